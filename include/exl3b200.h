@@ -1,0 +1,103 @@
+/*
+ * exl3b200.h -- C ABI of the B200 (sm_100a) EXL3 routed-expert MoE library (libexl3b200.so).
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a device address (or a host address the GPU can read
+ * through UVA: pinned, mapped host memory) unless stated.  `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  All work is enqueued on `stream`; no entry point synchronises the host or allocates memory.
+ * Return value: 0 = OK, 1 = invalid argument (nothing was enqueued), 2 = CUDA launch error, 3 = unsupported.
+ * exl3b_last_error() gives the message of the calling thread's last failure.  Device-side errors (an index out of
+ * range that a kernel skipped, a bounded wait that gave up) set bits of a device status word read by
+ * exl3b_device_status().
+ *
+ * Each entry point names the reference interface it replaces (sybil-solutions/qwen38-flash-next-b70-offload,
+ * file:line); the torch op layer in exl3b200/ops.py maps the reference's op schemas onto these calls.
+ */
+#ifndef EXL3B200_H
+#define EXL3B200_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- misc ---------------------------------------------------------------------------------------------------- */
+const char* exl3b_last_error(void);
+int exl3b_abi_version(void);
+/* Device status word (bits: 1 bounds, 2 bounded wait gave up, 4 bad geometry); synchronises `stream`. */
+int exl3b_device_status(int* host_status, int clear, void* stream);
+
+/* Replaces blob_bytes(H, I, K) (kernels/moe-a8/exl3_moe.a8.sycl:1551, Geom :42-54), with one K per tensor. */
+int64_t exl3b_blob_bytes(int H, int I, int Kg, int Ku, int Kd);
+
+/* ---- dequant ------------------------------------------------------------------------------------------------- */
+/* Replaces exl3_reconstruct(trellis, w, n0, K, cb=mul1) (experimental/n111-victim-ring/csrc/exl3_ops.sycl:539-555,
+ * ReconstructKernel kernels/moe-a8/exl3_esimd.h:869-936): tile matrix -> fp16 W_inner [rows16*16][ntiles*16] (ld ldw).
+ * Row r of the tile matrix starts at words + r*row_stride_words; tiles tile0..tile0+ntiles-1 are decoded.
+ * planar = 1: PLANAR4 rows (the expert blob, moe_offload.py:68-73; tile0 % 4 == 0), 0: plain checkpoint order. */
+int exl3b_dequant(const void* words, int rows16, int64_t row_stride_words, int tile0, int ntiles, int K, int planar,
+                  void* w_fp16, int64_t ldw, void* stream);
+/* Dequantise one projection of an expert blob: proj 0 gate / 1 up -> [H][I], 2 down -> [I][H] (fp16). */
+int exl3b_blob_dequant(const void* blob, int H, int I, int Kg, int Ku, int Kd, int proj, void* w_fp16, void* stream);
+
+/* ---- router -------------------------------------------------------------------------------------------------- */
+/* Replaces SGLang's TopK as consumed by Exl3XpuMoEMethod.apply (plugin/sglang_plugin.tier.py:534-535, 560):
+ * logits = x . Wr^T (+ bias) with the fixed fp32 order documented in csrc/exl3b_router.cu, softmax top-k (ties to the
+ * lower id), weights renormalised.  x, Wr bf16; ids int32 [T][topk]; w fp32 [T][topk]; logits fp32 [T][E] scratch. */
+int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias, int T, int H,
+                      int E, int topk, int32_t* ids, float* w, float* logits, void* stream);
+
+/* ---- device expert cache ------------------------------------------------------------------------------------- */
+/* Replaces launch_ensure (kernels/moe-a8/exl3_moe.a8.sycl:837-1040) as called by moe_forward_cached (:1229-1261)
+ * and moe_prefetch (:1194-1219), with the tier mask of moe_set_tier (:775-780) and victims of moe_set_victims
+ * (:768).  Deterministic rule: masked picks logged in ascending pick order; misses in ascending expert id; victims =
+ * the smallest (slot_last + 1, slot) among slots with slot_last < tick; i-th miss <-> i-th victim in slot order.
+ * ids/w are rewritten in place for masked picks (ram_res != NULL).  prefetch = 1: tick not advanced, pf_slot[i]
+ * receives the slots, fill_all untouched.  vict (may be NULL): [n, (old_key | -1, slot) x n]. */
+int exl3b_ensure(int32_t* ids, float* w, int npairs, int layer, int E, int S, int64_t* ptrs_all, int32_t* slot_of,
+                 int32_t* slot_key, int32_t* slot_last, int32_t* tick, const int64_t* host_base, int64_t slot_base,
+                 int64_t blob, int64_t hstride, int64_t* fill_all, int32_t* fill_list, int max_fill, int prefetch,
+                 int32_t* pf_slot, const uint8_t* ram_res, int32_t* ring, int ring_cap, const int32_t* safe,
+                 int32_t* vict, void* stream);
+/* Replaces the GEMV write-through fill (GateUpKernel/DownKernel `fill`, exl3_moe.a8.sycl:155-162, 207, 289) and
+ * PrefetchCopyKernel (:1146-1165): copies each planned fill's blob from ptrs[e] (host tier) into its slot
+ * (fill[e], or slot_base + pf_slot[i]*blob).  max_fills bounds the grid (>= fill_list[0]). */
+int exl3b_fill_copy(const int32_t* fill_list, const int64_t* ptrs, const int64_t* fill, const int32_t* pf_slot,
+                    int64_t slot_base, int64_t blob, int max_fills, void* stream);
+/* Replaces VictimCopyKernel (exl3_moe.a8.sycl:1168-1189): victim slot -> its host address, ram_res[old] = 1. */
+int exl3b_victim_copy(const int32_t* vict, const int64_t* host_base, int64_t slot_base, int64_t blob, int E,
+                      int64_t hstride, uint8_t* ram_res, int max_victims, void* stream);
+/* Replaces the cache commit of CombineKernel (exl3_moe.a8.sycl:378-386) and moe_prefetch's table update
+ * (:1212-1218): ptrs[e] = fill[e], fill[e] = 0 (or ptrs[e] = slot_base + pf_slot[i]*blob when pf_slot != NULL). */
+int exl3b_commit(const int32_t* fill_list, int64_t* ptrs, int64_t* fill, const int32_t* pf_slot, int64_t slot_base,
+                 int64_t blob, void* stream);
+
+/* ---- routed MoE, decode (few tokens) ------------------------------------------------------------------------- */
+/* Replaces moe_forward_impl's GEMV path (exl3_moe.a8.sycl:1263-1314: GateUpKernel :121-260, DownKernel :264-368,
+ * CombineKernel :371-395) for M tokens (any M; intended for M <= 64): out[m] = sum_k w[m,k] * expert(ids[m,k])(x[m]).
+ * x fp16 (x_bf16 = 0) or bf16 [M][x_stride]; ids int32 / w fp32 [M][topk] contiguous; ptrs int64 [E] blob
+ * addresses; kinfo (NULL = uniform K) int32 [E] per-expert Kg | Ku << 4 | Kd << 8; out like x.
+ * flags bit 0: skip picks whose weight is exactly 0 (tier-masked picks; the output is unchanged).
+ * workspace: >= exl3b_moe_decode_workspace(M, topk, H, I) bytes, 256-byte aligned, owned by the caller. */
+int64_t exl3b_moe_decode_workspace(int M, int topk, int H, int I);
+int exl3b_moe_decode(const void* x, int64_t x_stride, int x_bf16, const int32_t* ids, const float* w, int M, int topk,
+                     const int64_t* ptrs, const int32_t* kinfo, int H, int I, int K, int E, void* out,
+                     int64_t out_stride, int out_bf16, void* workspace, int64_t ws_bytes, int flags, void* stream);
+/* Profiling hook (no reference counterpart; the reference times graph replays from the host,
+ * plugin/sglang_plugin.tier.py:1036-1087): cudaEvent_t handles recorded by exl3b_moe_decode before its route
+ * prep, gate-up and down kernels and after down.  NULL disables a slot.  Process-global, off by default. */
+int exl3b_set_profile_events(void* before_route, void* before_gateup, void* before_down, void* after_down);
+
+/* ---- routing tables ------------------------------------------------------------------------------------------ */
+/* Replaces launch_align / moe_align (kernels/moe-a8/exl3_moe.a8.sycl:639-680, 1317-1325; buffers as make_route
+ * :744-757): picks bucketed by expert with a stable counting sort (ascending pick index inside an expert).
+ * ib int32 = [act_expert A | act_start A | act_cnt A | act_pstart A | n_act 1 | pair_tok P | pair_of P | 16 |
+ * blk_a mxb | n_blk 1], pair_w fp32 [P]; A = min(P, E), mxb = ceil(P / pad) + A.
+ * scratch: >= exl3b_align_scratch(P, E) bytes of device memory. */
+int64_t exl3b_align_scratch(int P, int E);
+int exl3b_align(const int32_t* ids, const float* w, int P, int topk, int E, int pad, int32_t* ib, float* pair_w, int A,
+                int mxb, void* scratch, int64_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EXL3B200_H */

@@ -1,0 +1,136 @@
+// exl3b_router.cu -- router GEMV + softmax top-k (the SGLang TopK the reference plugin consumes at
+// plugin/sglang_plugin.tier.py:534-535, 560).
+//
+// Arithmetic (fixed so that expert ids are bit-exact against the CPU oracle):
+//   logit[t,e] = dot(x[t], Wr[e]) + bias[e]; dot = xor-butterfly (offsets 16,8,4,2,1) over 32 chunk partials, chunk
+//   c = k in [c*H/32, (c+1)*H/32) accumulated in ascending k with fp32 fma from 0.
+//   top-k: largest logits, ties to the lower expert id, descending order.
+//   w_i = expf(l_i - l_0) / sum_j expf(l_j - l_0) (softmax renormalised over the selection).
+#include "exl3b_common.cuh"
+#include "exl3b_capi_util.h"
+
+namespace exl3b {
+
+// One warp per expert, 8 experts per block; blockIdx.y = token chunk of TC tokens.  Lane c owns chunk c:
+// its slice of Wr[e] stays in registers across the chunk's tokens.
+template <int CL, int TC>
+__global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
+                                                            const __nv_bfloat16* __restrict__ wr,
+                                                            const float* __restrict__ bias, int T, int H, int E,
+                                                            float* __restrict__ logits) {
+    int lane = threadIdx.x & 31;
+    int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (e >= E) return;
+    constexpr int NV = CL / 8;   // uint4 (8 bf16) per chunk
+    uint4 wv[NV];
+    const uint4* wp = reinterpret_cast<const uint4*>(wr + (long long)e * H + lane * CL);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) wv[i] = __ldg(wp + i);
+    float b = bias ? bias[e] : 0.0f;
+    int t0 = blockIdx.y * TC;
+    for (int t = t0; t < min(T, t0 + TC); ++t) {
+        const uint4* xp = reinterpret_cast<const uint4*>(x + (long long)t * xs + lane * CL);
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            uint4 xv = __ldg(xp + i);
+            const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+            const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv[i]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float x0 = __uint_as_float(xw[j] << 16), x1 = __uint_as_float(xw[j] & 0xFFFF0000u);
+                float w0 = __uint_as_float(ww[j] << 16), w1 = __uint_as_float(ww[j] & 0xFFFF0000u);
+                acc = __fmaf_rn(x0, w0, acc);
+                acc = __fmaf_rn(x1, w1, acc);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) logits[(long long)t * E + e] = bias ? __fadd_rn(acc, b) : acc;
+    }
+}
+
+// One warp per token: top-k by repeated warp argmax (ties -> lower id), then the renormalised softmax.
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, int topk,
+                                                          int* __restrict__ ids, float* __restrict__ w) {
+    int lane = threadIdx.x & 31;
+    int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    constexpr int MAXJ = 32;   // E <= 1024
+    float v[MAXJ];
+    int nj = (E + 31) / 32;
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j) {
+        int e = lane + 32 * j;
+        v[j] = (j < nj && e < E) ? logits[(long long)t * E + e] : -INFINITY;
+    }
+    unsigned used = 0;   // bit j: expert lane + 32 j already selected
+    float sel_v[32];
+    int sel_e[32];
+    for (int k = 0; k < topk; ++k) {
+        float bv = -INFINITY;
+        int be = 0x7FFFFFFF;
+#pragma unroll
+        for (int j = 0; j < MAXJ; ++j) {
+            int e = lane + 32 * j;
+            bool ok = j < nj && e < E && !((used >> j) & 1u);
+            if (ok && (v[j] > bv || (v[j] == bv && e < be))) { bv = v[j]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        if ((be & 31) == lane) used |= 1u << (be >> 5);
+        if (k < 32) { sel_v[k] = bv; sel_e[k] = be; }
+    }
+    if (lane == 0) {
+        float s = 0.0f;
+        float ex[32];
+        for (int k = 0; k < topk; ++k) { ex[k] = expf(sel_v[k] - sel_v[0]); s += ex[k]; }
+        for (int k = 0; k < topk; ++k) {
+            ids[(long long)t * topk + k] = sel_e[k];
+            w[(long long)t * topk + k] = ex[k] / s;
+        }
+    }
+}
+
+}  // namespace exl3b
+
+using namespace exl3b;
+
+extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias,
+                                           int T, int H, int E, int topk, int32_t* ids, float* w, float* logits,
+                                           void* stream) {
+    EXL3B_CHECK(x_bf16 && wr_bf16 && ids && w && logits, "exl3b_router_topk: null pointer");
+    EXL3B_CHECK(H % 256 == 0 && H <= 4096, "exl3b_router_topk: H must be a multiple of 256, <= 4096");
+    EXL3B_CHECK(E >= 1 && E <= 1024, "exl3b_router_topk: 1 <= E <= 1024");
+    EXL3B_CHECK(topk >= 1 && topk <= 32 && topk <= E, "exl3b_router_topk: 1 <= topk <= min(32, E)");
+    EXL3B_CHECK(x_stride >= H && ((x_stride * 2) % 16) == 0, "exl3b_router_topk: row stride must be >= H, 16-byte multiple");
+    EXL3B_CHECK((((uintptr_t)x_bf16) & 15) == 0 && (((uintptr_t)wr_bf16) & 15) == 0, "exl3b_router_topk: 16-byte alignment");
+    if (T <= 0) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    constexpr int TC = 8;
+    dim3 g1((E + 7) / 8, (T + TC - 1) / TC);
+    const __nv_bfloat16* xp = (const __nv_bfloat16*)x_bf16;
+    const __nv_bfloat16* wp = (const __nv_bfloat16*)wr_bf16;
+    switch (H / 32) {
+        case 8: router_logits_kernel<8, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 16: router_logits_kernel<16, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 24: router_logits_kernel<24, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 32: router_logits_kernel<32, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 40: router_logits_kernel<40, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 48: router_logits_kernel<48, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 56: router_logits_kernel<56, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 64: router_logits_kernel<64, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 80: router_logits_kernel<80, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 96: router_logits_kernel<96, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        case 128: router_logits_kernel<128, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+        default: return exl3b_fail(EXL3B_EINVAL, "exl3b_router_topk: unsupported H");
+    }
+    int rc = exl3b_launch_status("exl3b_router_topk(logits)");
+    if (rc) return rc;
+    router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, T, E, topk, ids, w);
+    return exl3b_launch_status("exl3b_router_topk(select)");
+}

@@ -1,0 +1,352 @@
+"""torch ops with the reference's schemas (namespace exl3b200_moe), backed by libexl3b200.so.
+
+The schemas are those of TORCH_LIBRARY(exl3xpu_moe) (kernels/moe-a8/exl3_moe.a8.sycl:1555-1592); only the namespace
+and the device (CUDA) differ.  Every CUDA implementation calls the C ABI on the current stream; nothing syncs the
+host, so the ops can be captured in CUDA graphs.  Process-global settings mirror the reference's moe_set_* setters
+(:682-790): they are read at call time (and therefore baked into captured graphs), and are not thread-safe.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream
+
+NS = "exl3b200_moe"
+
+
+class _Globals:
+    prefill_min_m = 256        # moe_set_prefill_min_m (exl3_moe.a8.sycl:787); M >= this: prefill path
+    pair_max_m = 4             # moe_set_pair_max_m (:730); accepted for schema compatibility
+    gu_p, dn_p = 5, 0          # moe_set_splits (:684); tuning knobs of the B70 kernels, accepted and ignored
+    mr = 0                     # moe_set_mr (:733)
+    debug = 0                  # moe_set_debug (:731)
+    host_stride = 0            # moe_set_host_stride (:772); 0 = blob size
+    ram_res = None             # moe_set_tier (:775-780): uint8 [L*E], int32 miss ring [1+R], int32 safe [L]
+    ring = None
+    safe = None
+    vict = None                # moe_set_victims (:767-768): int32 [1 + 2E]
+    skip_zero = True           # picks with weight 0 contribute 0: skip them (output unchanged)
+
+
+G = _Globals()
+
+
+def blob_bytes(H: int, I: int, K: int, Ku: int | None = None, Kd: int | None = None) -> int:
+    Ku = K if Ku is None else Ku
+    Kd = K if Kd is None else Kd
+    return int(_lib.lib().exl3b_blob_bytes(H, I, K, Ku, Kd))
+
+
+# ------------------------------------------------------------------------------------------------ building blocks
+def _check_x(x: torch.Tensor):
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise RuntimeError("exl3b200: x must be 2-D with unit column stride")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError("exl3b200: x must be bf16 or fp16")
+    if not x.is_cuda:
+        raise RuntimeError("exl3b200: x must be a CUDA tensor")
+
+
+def _check_route(ids: torch.Tensor, w: torch.Tensor):
+    if ids.dtype != torch.int32 or not ids.is_contiguous():
+        raise RuntimeError("exl3b200: topk_ids must be contiguous int32")
+    if w.dtype != torch.float32 or not w.is_contiguous():
+        raise RuntimeError("exl3b200: topk_w must be contiguous fp32")
+
+
+def moe_decode(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, ptrs: torch.Tensor, I: int, K: int, E: int,
+               kinfo: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed MoE through the decode kernels (any M; sized for small M)."""
+    _check_x(x)
+    _check_route(ids, w)
+    if ptrs.dtype != torch.int64 or not ptrs.is_contiguous():
+        raise RuntimeError("exl3b200: ptrs must be contiguous int64")
+    M, H = x.shape
+    topk = ids.shape[1] if ids.dim() == 2 else 1
+    if out is None:
+        out = torch.empty_like(x)
+    if M == 0:
+        return out
+    L = _lib.lib()
+    wsb = int(L.exl3b_moe_decode_workspace(M, topk, H, I))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
+    flags = 1 if G.skip_zero else 0
+    check(L.exl3b_moe_decode(x.data_ptr(), x.stride(0), int(x.dtype == torch.bfloat16), ids.data_ptr(), w.data_ptr(),
+                             M, topk, ptrs.data_ptr(), ptr(kinfo), H, I, K, E, out.data_ptr(), out.stride(0),
+                             int(out.dtype == torch.bfloat16), ws.data_ptr(), wsb, flags, stream(x.device)),
+          "moe_decode")
+    return out
+
+
+def router_topk(x: torch.Tensor, wr: torch.Tensor, bias: torch.Tensor | None, topk: int):
+    """Router GEMV + softmax top-k: returns (ids int32 [T, topk], w fp32 [T, topk])."""
+    if x.dtype != torch.bfloat16 or wr.dtype != torch.bfloat16:
+        raise RuntimeError("exl3b200 router: x and Wr must be bf16")
+    if x.dim() != 2 or x.stride(1) != 1 or not wr.is_contiguous():
+        raise RuntimeError("exl3b200 router: x 2-D unit-stride rows, Wr contiguous")
+    T, H = x.shape
+    E = wr.shape[0]
+    ids = torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    logits = torch.empty((T, E), dtype=torch.float32, device=x.device)
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise RuntimeError("exl3b200 router: bias must be contiguous fp32")
+    check(_lib.lib().exl3b_router_topk(x.data_ptr(), x.stride(0), wr.data_ptr(), ptr(bias), T, H, E, topk,
+                                       ids.data_ptr(), w.data_ptr(), logits.data_ptr(), stream(x.device)), "router")
+    return ids, w
+
+
+def dequant(words: torch.Tensor, rows16: int, row_stride: int, tile0: int, ntiles: int, K: int, planar: bool,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty((rows16 * 16, ntiles * 16), dtype=torch.float16, device=words.device)
+    check(_lib.lib().exl3b_dequant(words.data_ptr(), rows16, row_stride, tile0, ntiles, K, int(planar),
+                                   out.data_ptr(), out.stride(0), stream(words.device)), "dequant")
+    return out
+
+
+def blob_dequant(blob: torch.Tensor, H: int, I: int, Kg: int, Ku: int, Kd: int, proj: int) -> torch.Tensor:
+    shape = (H, I) if proj < 2 else (I, H)
+    out = torch.empty(shape, dtype=torch.float16, device=blob.device)
+    check(_lib.lib().exl3b_blob_dequant(blob.data_ptr(), H, I, Kg, Ku, Kd, proj, out.data_ptr(), stream(blob.device)),
+          "blob_dequant")
+    return out
+
+
+def ensure(ids, w, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob, fill_all,
+           fill_list, max_fill, prefetch=False, pf_slot=None, tier=True, vict=None):
+    """Device cache step (launch_ensure); tier mask / victims from the process globals when `tier`."""
+    S = slot_key.numel()
+    rr = G.ram_res if (tier and not prefetch) else None
+    check(_lib.lib().exl3b_ensure(ids.data_ptr(), ptr(w), ids.numel(), layer, E, S, ptrs_all.data_ptr(),
+                                  slot_of.data_ptr(), ptr(slot_key), ptr(slot_last), tick.data_ptr(),
+                                  host_base.data_ptr(), slot_base, blob, G.host_stride or blob, ptr(fill_all),
+                                  fill_list.data_ptr(), max_fill, int(prefetch), ptr(pf_slot), ptr(rr),
+                                  ptr(G.ring if rr is not None else None),
+                                  (G.ring.numel() - 1) if rr is not None else 0,
+                                  ptr(G.safe if rr is not None else None), ptr(vict), stream(ids.device)), "ensure")
+
+
+# ------------------------------------------------------------------------------------------------ reference ops
+def _moe_forward_impl(x, topk_ids, topk_w, ptrs, I, K, n_experts):
+    if x.shape[0] == 0:
+        return torch.empty_like(x)
+    return moe_decode(x, topk_ids, topk_w, ptrs, I, K, n_experts)
+
+
+def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
+                             slot_base, fill_all, fill_list, max_fill, I, K, n_experts, pend, done_seq):
+    if ptrs_all.dtype != torch.int64 or fill_all.dtype != torch.int64 or slot_of.dtype != torch.int32:
+        raise RuntimeError("exl3b200 moe_forward_cached: int64 ptrs_all / fill_all, int32 slot_of")
+    E = n_experts
+    M = x.shape[0]
+    ptrs_l = ptrs_all.narrow(0, layer * E, E)
+    if M == 0 or M >= G.prefill_min_m or slot_key.numel() == 0:
+        return _moe_forward_impl(x, topk_ids, topk_w, ptrs_l, I, K, E)
+    if pend.numel() and done_seq.numel():
+        raise RuntimeError("exl3b200 moe_forward_cached: copy-engine prefetch commits (pend/done_seq) not available")
+    _check_route(topk_ids, topk_w)
+    H = x.shape[1]
+    blob = blob_bytes(H, I, K)
+    npairs = topk_ids.numel()
+    mf = min(max_fill, E)
+    vict = G.vict
+    ensure(topk_ids, topk_w, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob,
+           fill_all, fill_list, mf, vict=vict)
+    L = _lib.lib()
+    s = stream(x.device)
+    nmax = min(mf, npairs)
+    fill_l = fill_all.narrow(0, layer * E, E)
+    if vict is not None and nmax > 0:
+        check(L.exl3b_victim_copy(vict.data_ptr(), host_base.data_ptr(), slot_base, blob, E, G.host_stride or blob,
+                                  ptr(G.ram_res), nmax, s), "victim_copy")
+    if nmax > 0:
+        check(L.exl3b_fill_copy(fill_list.data_ptr(), ptrs_l.data_ptr(), fill_l.data_ptr(), None, slot_base, blob,
+                                nmax, s), "fill_copy")
+    check(L.exl3b_commit(fill_list.data_ptr(), ptrs_l.data_ptr(), fill_l.data_ptr(), None, slot_base, blob, s),
+          "commit")
+    return moe_decode(x, topk_ids, topk_w, ptrs_l, I, K, E)
+
+
+def _moe_prefetch_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base, slot_base, pf_list,
+                       pf_slot, max_fill, n_experts, blob):
+    """Claim LRU slots for predicted experts (tick not advanced), copy them from host, repoint the table
+    (moe_prefetch, exl3_moe.a8.sycl:1194-1219)."""
+    if ids.dtype != torch.int32 or not ids.is_contiguous():
+        raise RuntimeError("exl3b200 moe_prefetch: contiguous int32 ids")
+    E, S = n_experts, slot_key.numel()
+    if S == 0 or ids.numel() == 0:
+        return
+    mf = min(max_fill, pf_slot.numel())
+    ensure(ids, None, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob, None,
+           pf_list, mf, prefetch=True, pf_slot=pf_slot, tier=False)
+    L = _lib.lib()
+    s = stream(ids.device)
+    ptrs_l = ptrs_all.narrow(0, layer * E, E)
+    nmax = min(mf, ids.numel())
+    if nmax > 0:
+        check(L.exl3b_fill_copy(pf_list.data_ptr(), ptrs_l.data_ptr(), None, pf_slot.data_ptr(), slot_base, blob, nmax,
+                                s), "prefetch copy")
+    check(L.exl3b_commit(pf_list.data_ptr(), ptrs_l.data_ptr(), None, pf_slot.data_ptr(), slot_base, blob, s),
+          "prefetch commit")
+
+
+def align(topk_ids: torch.Tensor, topk_w: torch.Tensor, n_experts: int, pad: int):
+    """Routing tables (launch_align, exl3_moe.a8.sycl:639-680): returns (ib int32, fb fp32) laid out as make_route
+    (:744-757): ib = [act_expert A | act_start A | act_cnt A | act_pstart A | n_act 1 | pair_tok P | pair_of P |
+    pad 16 | blk_a mxb | n_blk 1], fb = pair_w [P], with A = min(P, E), mxb = ceil(P/pad) + A."""
+    _check_route(topk_ids, topk_w)
+    P = topk_ids.numel()
+    topk = topk_ids.shape[-1] if topk_ids.dim() else 1
+    E = n_experts
+    A = min(P, E)
+    mxb = (P + pad - 1) // pad + A
+    dev = topk_ids.device
+    ib = torch.empty(4 * A + 1 + 2 * P + 16 + mxb + 1, dtype=torch.int32, device=dev)
+    fb = torch.empty(max(P, 1), dtype=torch.float32, device=dev)
+    L = _lib.lib()
+    nblk = (P + 1023) // 1024
+    scratch = torch.empty(max(int(L.exl3b_align_scratch(P, E)), 256), dtype=torch.uint8, device=dev)
+    check(L.exl3b_align(topk_ids.data_ptr(), topk_w.data_ptr(), P, topk, E, pad, ib.data_ptr(), fb.data_ptr(), A, mxb,
+                        scratch.data_ptr(), scratch.numel(), stream(dev)), "align")
+    del nblk
+    return ib, fb
+
+
+def _moe_align_impl(topk_ids, topk_w, n_experts, pad):
+    """Debug op moe_align (exl3_moe.a8.sycl:1317-1325) -> [int32 buf, fp32 buf]."""
+    ib, fb = align(topk_ids, topk_w, n_experts, pad)
+    return [ib, fb]
+
+
+def host_alloc(nbytes: int) -> torch.Tensor:
+    """Pinned host memory readable by the GPU at the same address (host_alloc, exl3_moe.a8.sycl:1529-1536)."""
+    return torch.empty(int(nbytes), dtype=torch.uint8, pin_memory=True)
+
+
+def usm_kind(p: int) -> int:
+    """0 unknown/pageable, 1 pinned host, 2 device, 3 managed (usm_kind, exl3_moe.a8.sycl:1539-1543)."""
+    return _usm_kind_cudart(p)
+
+
+def _usm_kind_cudart(p: int) -> int:
+    import ctypes
+    try:
+        rt = ctypes.CDLL("libcudart.so.12")
+    except OSError:
+        rt = ctypes.CDLL("libcudart.so")
+
+    class Attr(ctypes.Structure):
+        _fields_ = [("type", ctypes.c_int), ("device", ctypes.c_int), ("devicePointer", ctypes.c_void_p),
+                    ("hostPointer", ctypes.c_void_p)]
+
+    a = Attr()
+    if rt.cudaPointerGetAttributes(ctypes.byref(a), ctypes.c_void_p(p)) != 0:
+        rt.cudaGetLastError()
+        return 0
+    return {0: 0, 1: 1, 2: 2, 3: 3}.get(a.type, 0)
+
+
+def memcpy_async(dst: int, src: int, nbytes: int) -> None:
+    """Async raw copy on the current stream (memcpy_async, exl3_moe.a8.sycl:1546-1549)."""
+    import ctypes
+    try:
+        rt = ctypes.CDLL("libcudart.so.12")
+    except OSError:
+        rt = ctypes.CDLL("libcudart.so")
+    rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    rc = rt.cudaMemcpyAsync(ctypes.c_void_p(dst), ctypes.c_void_p(src), ctypes.c_size_t(nbytes), 4,
+                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc != 0:
+        raise RuntimeError(f"exl3b200 memcpy_async: cudaMemcpyAsync failed ({rc})")
+
+
+# setters (process globals)
+def moe_set_splits(gu_p: int, dn_p: int) -> None: G.gu_p, G.dn_p = int(gu_p), int(dn_p)
+def moe_set_mr(mr: int) -> None: G.mr = int(mr)
+def moe_set_debug(v: int) -> None: G.debug = int(v)
+def moe_set_pair_max_m(v: int) -> None: G.pair_max_m = int(v)
+def moe_set_prefill_min_m(v: int) -> None: G.prefill_min_m = int(v)
+def moe_set_host_stride(s: int) -> None: G.host_stride = int(s)
+
+
+def moe_set_victims(v: torch.Tensor) -> None:
+    G.vict = v if v.numel() else None
+
+
+def moe_set_tier(ram_res: torch.Tensor, miss: torch.Tensor, safe: torch.Tensor) -> None:
+    if ram_res.numel() == 0:
+        G.ram_res = G.ring = G.safe = None
+        return
+    if ram_res.dtype != torch.uint8 or miss.dtype != torch.int32 or safe.dtype != torch.int32:
+        raise RuntimeError("exl3b200 moe_set_tier: uint8 ram_res, int32 miss ring, int32 safe")
+    if miss.numel() < 2:
+        raise RuntimeError("exl3b200 moe_set_tier: the miss ring needs >= 1 entry")
+    G.ram_res, G.ring, G.safe = ram_res, miss, safe
+
+
+def moe_svm_prefetch(ptrs: torch.Tensor, nbytes: int, like: torch.Tensor) -> None:
+    """The reference maps RAM-tier pages for the GPU ahead of first touch (SVM); pinned host memory on CUDA is
+    always mapped, so there is nothing to do."""
+    return None
+
+
+# ------------------------------------------------------------------------------------------------ registration
+_registered = False
+
+
+def register() -> None:
+    """Define the torch ops (torch.ops.exl3b200_moe.*) once."""
+    global _registered
+    if _registered:
+        return
+    _lib.lib()   # fail loudly now if the library is missing
+    lib = torch.library.Library(NS, "DEF")
+    lib.define("moe_forward(Tensor x, Tensor topk_ids, Tensor topk_w, Tensor ptrs, int I, int K, int n_experts) -> Tensor")
+    lib.define("moe_forward_cached(Tensor x, Tensor topk_ids, Tensor topk_w, Tensor(a!) ptrs_all, int layer, "
+               "Tensor(b!) slot_of, Tensor(c!) slot_key, Tensor(d!) slot_last, Tensor(e!) tick, Tensor host_base, "
+               "int slot_base, Tensor(f!) fill_all, Tensor(g!) fill_list, int max_fill, int I, int K, int n_experts, "
+               "Tensor(h!) pend, Tensor done_seq) -> Tensor")
+    lib.define("moe_prefetch(Tensor ids, Tensor(a!) ptrs_all, int layer, Tensor(b!) slot_of, Tensor(c!) slot_key, "
+               "Tensor(d!) slot_last, Tensor tick, Tensor host_base, int slot_base, Tensor(e!) pf_list, "
+               "Tensor(f!) pf_slot, int max_fill, int n_experts, int blob) -> ()")
+    lib.define("moe_align(Tensor topk_ids, Tensor topk_w, int n_experts, int pad) -> Tensor[]")
+    lib.define("router_topk(Tensor x, Tensor wr, Tensor? bias, int topk) -> (Tensor, Tensor)")
+    lib.define("moe_forward_mixed(Tensor x, Tensor topk_ids, Tensor topk_w, Tensor ptrs, Tensor kinfo, int I, "
+               "int n_experts) -> Tensor")
+    lib.impl("moe_forward", _moe_forward_impl, "CUDA")
+    lib.impl("moe_forward_cached", _moe_forward_cached_impl, "CUDA")
+    lib.impl("moe_prefetch", _moe_prefetch_impl, "CUDA")
+    lib.impl("moe_align", _moe_align_impl, "CUDA")
+    lib.impl("router_topk", lambda x, wr, bias, topk: router_topk(x, wr, bias, topk), "CUDA")
+    lib.impl("moe_forward_mixed",
+             lambda x, ids, w, ptrs, kinfo, I, E: moe_decode(x, ids, w, ptrs, I, 0, E, kinfo=kinfo), "CUDA")
+
+    torch.library.register_fake(f"{NS}::moe_forward", lambda x, *a: torch.empty_like(x), lib=lib)
+    torch.library.register_fake(f"{NS}::moe_forward_cached", lambda x, *a: torch.empty_like(x), lib=lib)
+    torch.library.register_fake(f"{NS}::moe_forward_mixed", lambda x, *a: torch.empty_like(x), lib=lib)
+    globals()["_torch_lib"] = lib
+    _registered = True
+
+
+class _Ops:
+    """Namespace object mirroring torch.ops.exl3xpu_moe: tensor ops dispatch through torch, the rest are plain."""
+
+    def __getattr__(self, name):
+        register()
+        if hasattr(torch.ops.exl3b200_moe, name) and name in ("moe_forward", "moe_forward_cached", "moe_prefetch",
+                                                               "moe_align", "router_topk", "moe_forward_mixed"):
+            return getattr(torch.ops.exl3b200_moe, name)
+        fn = {"host_alloc": host_alloc, "usm_kind": usm_kind, "memcpy_async": memcpy_async,
+              "blob_bytes": blob_bytes, "moe_set_splits": moe_set_splits, "moe_set_mr": moe_set_mr,
+              "moe_set_debug": moe_set_debug, "moe_set_pair_max_m": moe_set_pair_max_m,
+              "moe_set_prefill_min_m": moe_set_prefill_min_m, "moe_set_victims": moe_set_victims,
+              "moe_set_tier": moe_set_tier, "moe_set_host_stride": moe_set_host_stride,
+              "moe_svm_prefetch": moe_svm_prefetch}.get(name)
+        if fn is None:
+            raise AttributeError(name)
+        return fn
+
+
+OPS = _Ops()

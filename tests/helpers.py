@@ -1,0 +1,56 @@
+"""Shared test helpers: synthetic layers on the device, oracle inputs, tolerance checks."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from exl3b200 import synth
+
+ATOL = 2e-2      # north-star layer tolerance: max-abs 2e-2 ...
+RTOL_L2 = 1e-3   # ... and rel-L2 1e-3 on bf16 outputs
+
+
+def make_layer(E, H, I, K, seed, device="cuda", kinfo=None, layer=0):
+    """Blobs [E, blob] uint8 on `device` (contiguous, one arena) and the int64 pointer table."""
+    if kinfo is None:
+        bb = synth.blob_geometry(H, I, K, K, K)["blob"]
+        blobs = torch.empty((E, bb), dtype=torch.uint8, device=device)
+        for e in range(E):
+            synth.fill_blob(blobs[e], seed, layer * E + e, H, I, K)
+        ptrs = blobs.data_ptr() + torch.arange(E, dtype=torch.int64) * bb
+        return blobs, ptrs.to(device), [blobs[e] for e in range(E)]
+    parts = []
+    for e in range(E):
+        kg, ku, kd = kinfo[e]
+        parts.append(synth.make_blob(seed, layer * E + e, H, I, kg, ku, kd, device=device))
+    sizes = [p.numel() for p in parts]
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]])
+    arena = torch.empty(int(sum(sizes)), dtype=torch.uint8, device=device)
+    for p, o in zip(parts, offs):
+        arena[int(o):int(o) + p.numel()].copy_(p)
+    ptrs = arena.data_ptr() + torch.tensor(offs, dtype=torch.int64)
+    return arena, ptrs.to(device), [arena[int(o):int(o) + s] for o, s in zip(offs, sizes)]
+
+
+def oracle_blobs(views, ids: np.ndarray):
+    need = set(int(e) for e in np.asarray(ids).ravel())
+    return [views[e].cpu().numpy() if e in need else None for e in range(len(views))]
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def assert_close_layer(got_bits: np.ndarray, ref_bits: np.ndarray, atol=ATOL, rl2=RTOL_L2):
+    g = bf16_to_f32(got_bits).astype(np.float64)
+    r = bf16_to_f32(ref_bits).astype(np.float64)
+    assert np.all(np.isfinite(g)), "non-finite output"
+    mad = float(np.abs(g - r).max()) if g.size else 0.0
+    den = float(np.linalg.norm(r)) or 1.0
+    rel = float(np.linalg.norm(g - r)) / den
+    assert mad <= atol and rel <= rl2, f"max-abs {mad:.3g} (tol {atol}), rel-L2 {rel:.3g} (tol {rl2})"
+    return mad, rel

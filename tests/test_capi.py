@@ -1,0 +1,67 @@
+"""CPU: the C-ABI library loads, exports every symbol include/exl3b200.h declares, and rejects bad arguments before
+launching anything (no compute runs here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from exl3b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "exl3b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(exl3b_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "exl3b_moe_decode" in names and "exl3b_ensure" in names and len(names) >= 14
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert set(declared()) <= set(_lib.exported_symbols())
+
+
+def test_blob_bytes_and_abi():
+    L = _lib.lib()
+    assert L.exl3b_abi_version() == 1
+    assert L.exl3b_blob_bytes(2048, 768, 3, 3, 3) == 1786368
+    assert L.exl3b_blob_bytes(2560, 640, 3, 3, 3) == 1862400
+    assert L.exl3b_moe_decode_workspace(1, 10, 2048, 768) > 0
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.exl3b_dequant(None, 1, 24, 0, 4, 3, 1, None, 64, None),
+    lambda L: L.exl3b_dequant(1 << 20, 1, 24, 1, 4, 3, 1, 1 << 21, 64, None),      # planar tile0 % 4
+    lambda L: L.exl3b_dequant(1 << 20, 1, 24, 0, 4, 7, 0, 1 << 21, 64, None),      # K out of range
+    lambda L: L.exl3b_ensure(1 << 20, 1 << 20, 10, 0, 2000, 8, 1 << 20, 1 << 20, 1 << 20, 1 << 20, 1 << 20, 1 << 20,
+                             0, 64, 64, 1 << 20, 1 << 20, 8, 0, None, None, None, 0, None, None, None),  # E > 1024
+    lambda L: L.exl3b_moe_decode(1 << 20, 2048, 1, 1 << 20, 1 << 20, 1, 10, 1 << 20, None, 2000, 768, 3, 512,
+                                 1 << 20, 2048, 1, 1 << 20, 1 << 30, 1, None),    # H % 128
+    lambda L: L.exl3b_moe_decode(1 << 20, 2048, 1, 1 << 20, 1 << 20, 1, 10, 1 << 20, None, 2048, 768, 3, 512,
+                                 1 << 20, 2048, 1, 1 << 20, 16, 1, None),          # workspace too small
+    lambda L: L.exl3b_router_topk(1 << 20, 2048, 1 << 20, None, 1, 2048, 512, 40, 1 << 20, 1 << 20, 1 << 20, None),
+    lambda L: L.exl3b_align(1 << 20, 1 << 20, 10, 10, 512, 32, 1 << 20, 1 << 20, 9, 10, 1 << 20, 1 << 20, None),
+])
+def test_invalid_arguments_rejected_before_launch(call):
+    L = _lib.lib()
+    assert call(L) == 1
+    assert L.exl3b_last_error()
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.lib()
