@@ -75,7 +75,8 @@ int exl3b_commit(const int32_t* fill_list, int64_t* ptrs, int64_t* fill, const i
 /* Replaces moe_forward_impl's GEMV path (exl3_moe.a8.sycl:1263-1314: GateUpKernel :121-260, DownKernel :264-368,
  * CombineKernel :371-395) for M tokens (any M; intended for M <= 64): out[m] = sum_k w[m,k] * expert(ids[m,k])(x[m]).
  * x fp16 (x_bf16 = 0) or bf16 [M][x_stride]; ids int32 / w fp32 [M][topk] contiguous; ptrs int64 [E] blob
- * addresses; kinfo (NULL = uniform K) int32 [E] per-expert Kg | Ku << 4 | Kd << 8; out like x.
+ * addresses; kinfo (NULL = uniform K) int32 [E] per-expert Kg | Ku << 4 | Kd << 8; out [M][out_stride] with
+ * out_bf16 = 0 fp16, 1 bf16, 2 fp32 (the un-rounded layer output).
  * flags bit 0: skip picks whose weight is exactly 0 (tier-masked picks; the output is unchanged).
  * workspace: >= exl3b_moe_decode_workspace(M, topk, H, I) bytes, 256-byte aligned, owned by the caller. */
 int64_t exl3b_moe_decode_workspace(int M, int topk, int H, int I);

@@ -337,7 +337,10 @@ static void expert_forward(const uint16_t* x, int x_is_bf16, const uint8_t* blob
  */
 EXPORT void ora_moe_layer(const uint16_t* x, int x_is_bf16, const int32_t* ids, const float* w, int M, int topk,
                           const uint8_t* const* blobs, const int32_t* kinfo, int H, int I, int K, int out_bf16,
-                          uint16_t* out, float* y_out, uint16_t* abuf_out) {
+                          void* out_v, float* y_out, uint16_t* abuf_out) {
+    /* out_bf16: 0 fp16 bits, 1 bf16 bits, 2 fp32 (the layer output before its final rounding) */
+    uint16_t* out = (uint16_t*)out_v;
+    float* out_f = (float*)out_v;
     float* y = (float*)malloc((size_t)H * 4);
     float* acc = (float*)malloc((size_t)H * 4);
     uint16_t* abuf = (uint16_t*)malloc((size_t)I * 2);
@@ -359,8 +362,10 @@ EXPORT void ora_moe_layer(const uint16_t* x, int x_is_bf16, const int32_t* ids, 
             if (abuf_out) memcpy(abuf_out + ((size_t)m * topk + k) * I, abuf, (size_t)I * 2);
             for (int i = 0; i < H; ++i) acc[i] += y[i];
         }
-        for (int i = 0; i < H; ++i)
-            out[(size_t)m * H + i] = out_bf16 ? ora_f32_to_bf16(acc[i]) : ora_f32_to_f16(acc[i]);
+        for (int i = 0; i < H; ++i) {
+            if (out_bf16 == 2) out_f[(size_t)m * H + i] = acc[i];
+            else out[(size_t)m * H + i] = out_bf16 ? ora_f32_to_bf16(acc[i]) : ora_f32_to_f16(acc[i]);
+        }
     }
     free(y); free(acc); free(abuf); free(wg); free(wu); free(wd);
 }

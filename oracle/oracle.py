@@ -60,7 +60,7 @@ def lib():
             "ora_blob_dequant": (None, [vp, ci, ci, ci, ci, ci, ci, u16p]),
             "ora_fwht128": (None, [f32p]),
             "ora_had_in": (None, [u16p, ci, u16p, ci, u16p]),
-            "ora_moe_layer": (None, [u16p, ci, i32p, f32p, ci, ci, vp, vp, ci, ci, ci, ci, u16p, vp, vp]),
+            "ora_moe_layer": (None, [u16p, ci, i32p, f32p, ci, ci, vp, vp, ci, ci, ci, ci, vp, vp, vp]),
             "ora_dense_glu": (None, [u16p, ci, vp, ci, ci, ci, ci, ci, f32p]),
             "ora_router_dot": (ctypes.c_float, [u16p, u16p, ci]),
             "ora_router": (None, [u16p, u16p, vp, ci, ci, ci, ci, i32p, f32p, vp]),
@@ -140,22 +140,22 @@ def had_in(x_bits: np.ndarray, suh_bits: np.ndarray, x_is_bf16: bool = True) -> 
 
 # ---------------------------------------------------------------- layer
 def moe_layer(x_bits: np.ndarray, ids: np.ndarray, w: np.ndarray, blobs: list, H: int, I: int, K: int = 3,
-              kinfo: np.ndarray | None = None, x_is_bf16: bool = True, want_y: bool = False):
+              kinfo: np.ndarray | None = None, x_is_bf16: bool = True, want_y: bool = False, out_f32: bool = False):
     """Routed MoE layer.  x_bits: uint16 [M, H] (bf16 bits); blobs: list of uint8 arrays indexed by
-    expert id (None for unused ids); returns out bf16 bits [M, H] (and y fp32 [M*topk, H], abuf fp16
-    bits [M*topk, I] when want_y)."""
+    expert id (None for unused ids); returns out bf16 bits [M, H] (fp32 [M, H] before the final rounding when
+    out_f32), and y fp32 [M*topk, H], abuf fp16 bits [M*topk, I] when want_y."""
     x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     w = np.ascontiguousarray(w, dtype=np.float32)
     M, topk = ids.shape
     keep = [np.ascontiguousarray(b, dtype=np.uint8) if b is not None else None for b in blobs]
     arr = (ctypes.c_void_p * len(keep))(*[(b.ctypes.data if b is not None else 0) for b in keep])
-    out = np.empty((M, H), dtype=np.uint16)
+    out = np.empty((M, H), dtype=np.float32 if out_f32 else np.uint16)
     y = np.empty((M * topk, H), dtype=np.float32) if want_y else None
     ab = np.empty((M * topk, I), dtype=np.uint16) if want_y else None
     ki = np.ascontiguousarray(kinfo, dtype=np.int32) if kinfo is not None else None
     lib().ora_moe_layer(x_bits, int(x_is_bf16), ids, w, M, topk, ctypes.cast(arr, ctypes.c_void_p), _ptr(ki),
-                        H, I, K, 1, out, _ptr(y), _ptr(ab))
+                        H, I, K, 2 if out_f32 else 1, _ptr(out), _ptr(y), _ptr(ab))
     return (out, y, ab) if want_y else out
 
 

@@ -95,8 +95,8 @@ struct LaneWin {
 // low 16 bits are the fp16 bit pattern of 1024 + bytesum (exact); one fp16x2 fma applies c1, c2 with one rounding.
 __device__ __forceinline__ uint32_t mul1_pair(uint32_t st0, uint32_t st1) {
     uint32_t x0 = st0 * 0x83DCD12Du, x1 = st1 * 0x83DCD12Du;
-    uint32_t h0 = (uint32_t)__dp4a((int)x0, 0x01010101, 0x6400);
-    uint32_t h1 = (uint32_t)__dp4a((int)x1, 0x01010101, 0x6400);
+    uint32_t h0 = __dp4a(x0, 0x01010101u, 0x6400u);   // unsigned byte dot product: 0x6400 + sum of the 4 bytes
+    uint32_t h1 = __dp4a(x1, 0x01010101u, 0x6400u);
     uint32_t hp = h0 | (h1 << 16);
     __half2 h = *reinterpret_cast<__half2*>(&hp);
     const __half2 c1 = __halves2half2(__ushort_as_half((unsigned short)0x1eee), __ushort_as_half((unsigned short)0x1eee));

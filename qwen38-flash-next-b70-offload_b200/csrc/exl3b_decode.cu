@@ -106,7 +106,8 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(DecodeArgs a) {
     for (int m = 0; m < a.M; ++m) {
         if (a.tok_cnt[m] != 0) continue;
         for (int c = tid; c < a.H; c += blockDim.x) {
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + c] = __float2bfloat16(0.0f);
+            if (a.out_bf16 == 2) reinterpret_cast<float*>(a.out)[(long long)m * a.os + c] = 0.0f;
+            else if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + c] = __float2bfloat16(0.0f);
             else reinterpret_cast<__half*>(a.out)[(long long)m * a.os + c] = __float2half(0.0f);
         }
     }
@@ -368,7 +369,9 @@ __device__ void dn_unit(const DecodeArgs& a, int ent, int nbh, int kbi) {
                 s[0] += q4.x; s[1] += q4.y; s[2] += q4.z; s[3] += q4.w;
             }
             long long o = (long long)m * a.os + nbh * 128 + 4 * lane;
-            if (a.out_bf16) {
+            if (a.out_bf16 == 2) {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + o) = make_float4(s[0], s[1], s[2], s[3]);
+            } else if (a.out_bf16) {
                 __nv_bfloat162 p0 = __floats2bfloat162_rn(s[0], s[1]), p1 = __floats2bfloat162_rn(s[2], s[3]);
                 uint2 ov;
                 ov.x = *reinterpret_cast<uint32_t*>(&p0);
@@ -457,7 +460,9 @@ extern "C" EXL3B_API int exl3b_moe_decode(const void* x, int64_t x_stride, int x
     EXL3B_CHECK(topk >= 1 && M >= 0, "exl3b_moe_decode: bad M / topk");
     EXL3B_CHECK(x_stride >= H && out_stride >= H && (x_stride % 4) == 0 && (out_stride % 4) == 0,
                 "exl3b_moe_decode: row strides must be >= H and multiples of 4 elements");
-    EXL3B_CHECK((((uintptr_t)x) & 7) == 0 && (((uintptr_t)out) & 7) == 0, "exl3b_moe_decode: x/out 8-byte alignment");
+    EXL3B_CHECK((((uintptr_t)x) & 7) == 0 && (((uintptr_t)out) & (out_bf16 == 2 ? 15 : 7)) == 0,
+                "exl3b_moe_decode: x 8-byte / out 8-byte (fp32: 16-byte) alignment");
+    EXL3B_CHECK(out_bf16 >= 0 && out_bf16 <= 2, "exl3b_moe_decode: out dtype code 0 fp16, 1 bf16, 2 fp32");
     if (M == 0) return 0;
     WsLayout L = ws_layout(M, topk, H, I);
     EXL3B_CHECK(workspace && ws_bytes >= (int64_t)L.total, "exl3b_moe_decode: workspace too small");

@@ -39,6 +39,8 @@ def blob_bytes(H: int, I: int, K: int, Ku: int | None = None, Kd: int | None = N
 
 
 # ------------------------------------------------------------------------------------------------ building blocks
+_OUT_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
 def _check_x(x: torch.Tensor):
     if x.dim() != 2 or x.stride(1) != 1:
         raise RuntimeError("exl3b200: x must be 2-D with unit column stride")
@@ -74,7 +76,7 @@ def moe_decode(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, ptrs: torch.
     flags = 1 if G.skip_zero else 0
     check(L.exl3b_moe_decode(x.data_ptr(), x.stride(0), int(x.dtype == torch.bfloat16), ids.data_ptr(), w.data_ptr(),
                              M, topk, ptrs.data_ptr(), ptr(kinfo), H, I, K, E, out.data_ptr(), out.stride(0),
-                             int(out.dtype == torch.bfloat16), ws.data_ptr(), wsb, flags, stream(x.device)),
+                             _OUT_CODE[out.dtype], ws.data_ptr(), wsb, flags, stream(x.device)),
           "moe_decode")
     return out
 

@@ -9,7 +9,7 @@ import torch
 import oracle as O
 from exl3b200 import ExpertStore, ops as exops, synth
 from exl3b200 import ops as X
-from helpers import assert_close_layer, bits, make_layer, oracle_blobs
+from helpers import assert_close_f32, assert_close_layer, bits, make_layer, oracle_blobs
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -74,6 +74,21 @@ def test_router_bit_exact(T, with_bias):
 
 
 # ------------------------------------------------------------------------------------------------ decode layer
+def check_decode(x, ids, w, ptrs, views, H, I, K, E, kinfo=None):
+    """bf16 product output and fp32 layer output of the CUDA decode path against the oracle."""
+    xd, idd, wd = x.to(DEV), ids.to(DEV), w.to(DEV)
+    kd = kinfo.to(DEV) if kinfo is not None else None
+    out = X.moe_decode(xd, idd, wd, ptrs, I, K, E, kinfo=kd)
+    o32 = X.moe_decode(xd, idd, wd, ptrs, I, K, E, kinfo=kd,
+                       out=torch.empty(x.shape[0], H, dtype=torch.float32, device=DEV))
+    ki = kinfo.numpy() if kinfo is not None else None
+    blobs = oracle_blobs(views, ids.numpy())
+    ref = O.moe_layer(bits(x), ids.numpy(), w.numpy(), blobs, H, I, K or 3, kinfo=ki)
+    ref32 = O.moe_layer(bits(x), ids.numpy(), w.numpy(), blobs, H, I, K or 3, kinfo=ki, out_f32=True)
+    assert_close_f32(o32.cpu().numpy(), ref32)
+    return assert_close_layer(bits(out), ref)
+
+
 def _route(T, E, topk, seed):
     g = torch.Generator().manual_seed(seed)
     ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).to(torch.int32)
@@ -88,9 +103,7 @@ def test_decode_layer_small(T):
     blobs, ptrs, views = make_layer(E, H, I, K, seed=21)
     x = synth.activations(T, H, 5 + T)
     ids, w = _route(T, E, topk, T)
-    out = X.moe_decode(x.to(DEV), ids.to(DEV), w.to(DEV), ptrs, I, K, E)
-    ref = O.moe_layer(bits(x), ids.numpy(), w.numpy(), oracle_blobs(views, ids.numpy()), H, I, K)
-    assert_close_layer(bits(out), ref)
+    check_decode(x, ids, w, ptrs, views, H, I, K, E)
 
 
 @pytest.mark.parametrize("T", [1, 4])
@@ -101,11 +114,9 @@ def test_decode_layer_full_shape(T):
     x = synth.activations(T, H, 0)
     wr = synth.router_weight(E, H, 0.02, 0)
     ids, w = X.router_topk(x.to(DEV), wr.to(DEV), None, topk)
-    out = X.moe_decode(x.to(DEV), ids, w, ptrs, I, K, E)
     rid, rw, _ = O.router(bits(x), bits(wr), None, topk)
     assert np.array_equal(ids.cpu().numpy(), rid)
-    ref = O.moe_layer(bits(x), rid, rw, oracle_blobs(views, rid), H, I, K)
-    assert_close_layer(bits(out), ref)
+    check_decode(x, torch.from_numpy(rid), torch.from_numpy(rw), ptrs, views, H, I, K, E)
 
 
 def test_decode_mixed_k():
@@ -115,9 +126,7 @@ def test_decode_mixed_k():
     ki = torch.tensor([synth.kinfo_pack(*k) for k in kinfo], dtype=torch.int32)
     x = synth.activations(T, H, 9)
     ids, w = _route(T, E, topk, 4)
-    out = X.moe_decode(x.to(DEV), ids.to(DEV), w.to(DEV), ptrs, I, 0, E, kinfo=ki.to(DEV))
-    ref = O.moe_layer(bits(x), ids.numpy(), w.numpy(), oracle_blobs(views, ids.numpy()), H, I, 3, kinfo=ki.numpy())
-    assert_close_layer(bits(out), ref)
+    check_decode(x, ids, w, ptrs, views, H, I, 0, E, kinfo=ki)
 
 
 def test_zero_weight_picks_and_duplicates():
@@ -127,9 +136,8 @@ def test_zero_weight_picks_and_duplicates():
     x = synth.activations(T, H, 1)
     ids = torch.tensor([[1, 2, 0, 0], [3, 3, 3, 3], [5, 6, 7, 1]], dtype=torch.int32)
     w = torch.tensor([[0.5, 0.5, 0.0, 0.0], [0.0, 0.0, 0.0, 0.0], [0.1, 0.2, 0.3, 0.4]], dtype=torch.float32)
+    check_decode(x, ids, w, ptrs, views, H, I, K, E)
     out = X.moe_decode(x.to(DEV), ids.to(DEV), w.to(DEV), ptrs, I, K, E)
-    ref = O.moe_layer(bits(x), ids.numpy(), w.numpy(), oracle_blobs(views, ids.numpy()), H, I, K)
-    assert_close_layer(bits(out), ref)
     assert torch.all(out[1].float() == 0)
 
 
