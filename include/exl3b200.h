@@ -44,7 +44,10 @@ int exl3b_blob_dequant(const void* blob, int H, int I, int Kg, int Ku, int Kd, i
  * logits = x . Wr^T (+ bias) with the fixed fp32 order documented in csrc/exl3b_router.cu, softmax top-k (ties to the
  * lower id), weights renormalised.  x, Wr bf16; ids int32 [T][topk]; w fp32 [T][topk]; logits fp32 [T][E] scratch. */
 int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias, int T, int H,
-                      int E, int topk, int32_t* ids, float* w, float* logits, void* stream);
+                      int E, int topk, int32_t* ids, float* w, float* logits, int32_t* counter, void* stream);
+/* counter (may be NULL): int32 in device memory, zero before the first call, left at zero by every call; with it
+ * and T <= 8 the selection runs inside the logits kernel (last block to finish), else in a second kernel.
+ * Calls that share a counter must not overlap on the GPU. */
 
 /* ---- device expert cache ------------------------------------------------------------------------------------- */
 /* Replaces launch_ensure (kernels/moe-a8/exl3_moe.a8.sycl:837-1040) as called by moe_forward_cached (:1229-1261)
@@ -83,6 +86,18 @@ int64_t exl3b_moe_decode_workspace(int M, int topk, int H, int I);
 int exl3b_moe_decode(const void* x, int64_t x_stride, int x_bf16, const int32_t* ids, const float* w, int M, int topk,
                      const int64_t* ptrs, const int32_t* kinfo, int H, int I, int K, int E, void* out,
                      int64_t out_stride, int out_bf16, void* workspace, int64_t ws_bytes, int flags, void* stream);
+/* Replaces moe_forward_cached (kernels/moe-a8/exl3_moe.a8.sycl:1229-1261): the device cache step of exl3b_ensure
+ * (same state tensors, same deterministic rule, tier mask and victims), then the decode above on the layer's table
+ * ptrs_all + layer*E.  Cache fills are read from their host address during the call and copied into their slots; the
+ * table is repointed (commit) by the last block of the call.  ids / w are rewritten in place for masked picks.
+ * vict (may be NULL) enables the victim write-back (VictimCopyKernel) with vict_ram_res flags. */
+int exl3b_moe_decode_cached(const void* x, int64_t x_stride, int x_bf16, int32_t* ids, float* w, int M, int topk,
+                            int layer, int64_t* ptrs_all, int32_t* slot_of, int32_t* slot_key, int32_t* slot_last,
+                            int32_t* tick, const int64_t* host_base, int64_t slot_base, int64_t blob, int64_t hstride,
+                            int64_t* fill_all, int32_t* fill_list, int max_fill, int S, const uint8_t* ram_res,
+                            int32_t* ring, int ring_cap, const int32_t* safe, int32_t* vict, uint8_t* vict_ram_res,
+                            int H, int I, int K, int E, void* out, int64_t out_stride, int out_bf16, void* workspace,
+                            int64_t ws_bytes, int flags, void* stream);
 /* Profiling hook (no reference counterpart; the reference times graph replays from the host,
  * plugin/sglang_plugin.tier.py:1036-1087): cudaEvent_t handles recorded by exl3b_moe_decode before its route
  * prep, gate-up and down kernels and after down.  NULL disables a slot.  Process-global, off by default. */

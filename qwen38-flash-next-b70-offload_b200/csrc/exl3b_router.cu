@@ -8,8 +8,61 @@
 //   w_i = expf(l_i - l_0) / sum_j expf(l_j - l_0) (softmax renormalised over the selection).
 #include "exl3b_common.cuh"
 #include "exl3b_capi_util.h"
+#include "exl3b_launch.h"
 
 namespace exl3b {
+
+// One warp per token: top-k by repeated warp argmax (ties -> lower id), then the renormalised softmax.
+__device__ __forceinline__ void topk_warp(const float* __restrict__ logits, int t, int E, int topk, int* __restrict__ ids,
+                                          float* __restrict__ w) {
+    const int lane = threadIdx.x & 31;
+    constexpr int MAXJ = 32;   // E <= 1024
+    float v[MAXJ];
+    const int nj = (E + 31) / 32;
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j) {
+        int e = lane + 32 * j;
+        v[j] = (j < nj && e < E) ? __ldcg(logits + (long long)t * E + e) : -INFINITY;
+    }
+    unsigned used = 0;   // bit j: expert lane + 32 j already selected
+    float sv = 0.0f, s0 = 0.0f, ssum = 0.0f;
+    int se = 0;
+    for (int k = 0; k < topk; ++k) {
+        float bv = -INFINITY;
+        int be = 0x7FFFFFFF;
+#pragma unroll
+        for (int j = 0; j < MAXJ; ++j) {
+            int e = lane + 32 * j;
+            bool ok = j < nj && e < E && !((used >> j) & 1u);
+            if (ok && (v[j] > bv || (v[j] == bv && e < be))) { bv = v[j]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        if ((be & 31) == lane) used |= 1u << (be >> 5);
+        if (k == 0) s0 = bv;
+        if (lane == k) { sv = bv; se = be; }   // lane k keeps the k-th selection
+    }
+    // w_k = expf(l_k - l_0) / sum_j expf(l_j - l_0), the sum in selection order
+    float ex = (lane < topk) ? expf(sv - s0) : 0.0f;
+    for (int k = 0; k < topk; ++k) ssum += __shfl_sync(0xffffffffu, ex, k);
+    if (lane < topk) {
+        ids[(long long)t * topk + lane] = se;
+        w[(long long)t * topk + lane] = ex / ssum;
+    }
+}
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, int topk,
+                                                          int* __restrict__ ids, float* __restrict__ w) {
+    pdl_wait();
+    pdl_trigger();
+    int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    topk_warp(logits, t, E, topk, ids, w);
+}
 
 // One warp per expert, 8 experts per block; blockIdx.y = token chunk of TC tokens.  Lane c owns chunk c:
 // its slice of Wr[e] stays in registers across the chunk's tokens.
@@ -17,18 +70,23 @@ template <int CL, int TC>
 __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
                                                             const __nv_bfloat16* __restrict__ wr,
                                                             const float* __restrict__ bias, int T, int H, int E,
-                                                            float* __restrict__ logits) {
+                                                            float* __restrict__ logits, int topk, int* __restrict__ ids,
+                                                            float* __restrict__ w, int* counter) {
+    __shared__ int sh_last;
     int lane = threadIdx.x & 31;
     int e = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (e >= E) return;
     constexpr int NV = CL / 8;   // uint4 (8 bf16) per chunk
     uint4 wv[NV];
-    const uint4* wp = reinterpret_cast<const uint4*>(wr + (long long)e * H + lane * CL);
+    // the router weights do not depend on earlier kernels: load them before waiting for x
+    const int ec = e < E ? e : E - 1;
+    const uint4* wp = reinterpret_cast<const uint4*>(wr + (long long)ec * H + lane * CL);
 #pragma unroll
     for (int i = 0; i < NV; ++i) wv[i] = __ldg(wp + i);
-    float b = bias ? bias[e] : 0.0f;
+    float b = (bias && e < E) ? bias[e] : 0.0f;
+    pdl_wait();
+    pdl_trigger();
     int t0 = blockIdx.y * TC;
-    for (int t = t0; t < min(T, t0 + TC); ++t) {
+    for (int t = t0; e < E && t < min(T, t0 + TC); ++t) {
         const uint4* xp = reinterpret_cast<const uint4*>(x + (long long)t * xs + lane * CL);
         float acc = 0.0f;
 #pragma unroll
@@ -46,54 +104,22 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-        if (lane == 0) logits[(long long)t * E + e] = bias ? __fadd_rn(acc, b) : acc;
+        if (lane == 0) __stcg(logits + (long long)t * E + e, bias ? __fadd_rn(acc, b) : acc);
     }
-}
-
-// One warp per token: top-k by repeated warp argmax (ties -> lower id), then the renormalised softmax.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, int topk,
-                                                          int* __restrict__ ids, float* __restrict__ w) {
-    int lane = threadIdx.x & 31;
-    int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (t >= T) return;
-    constexpr int MAXJ = 32;   // E <= 1024
-    float v[MAXJ];
-    int nj = (E + 31) / 32;
-#pragma unroll
-    for (int j = 0; j < MAXJ; ++j) {
-        int e = lane + 32 * j;
-        v[j] = (j < nj && e < E) ? logits[(long long)t * E + e] : -INFINITY;
+    if (!counter) return;
+    // fused selection: the last block to finish runs the top-k of every token (T <= 8, one warp per token)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        int old = atomicAdd(counter, 1);
+        sh_last = old == (int)(gridDim.x * gridDim.y) - 1;
     }
-    unsigned used = 0;   // bit j: expert lane + 32 j already selected
-    float sel_v[32];
-    int sel_e[32];
-    for (int k = 0; k < topk; ++k) {
-        float bv = -INFINITY;
-        int be = 0x7FFFFFFF;
-#pragma unroll
-        for (int j = 0; j < MAXJ; ++j) {
-            int e = lane + 32 * j;
-            bool ok = j < nj && e < E && !((used >> j) & 1u);
-            if (ok && (v[j] > bv || (v[j] == bv && e < be))) { bv = v[j]; be = e; }
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            int oe = __shfl_xor_sync(0xffffffffu, be, o);
-            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-        }
-        if ((be & 31) == lane) used |= 1u << (be >> 5);
-        if (k < 32) { sel_v[k] = bv; sel_e[k] = be; }
-    }
-    if (lane == 0) {
-        float s = 0.0f;
-        float ex[32];
-        for (int k = 0; k < topk; ++k) { ex[k] = expf(sel_v[k] - sel_v[0]); s += ex[k]; }
-        for (int k = 0; k < topk; ++k) {
-            ids[(long long)t * topk + k] = sel_e[k];
-            w[(long long)t * topk + k] = ex[k] / s;
-        }
-    }
+    __syncthreads();
+    if (!sh_last) return;
+    __threadfence();
+    int t = threadIdx.x >> 5;
+    if (t < T) topk_warp(logits, t, E, topk, ids, w);
+    if (threadIdx.x == 0) *counter = 0;
 }
 
 }  // namespace exl3b
@@ -102,7 +128,7 @@ using namespace exl3b;
 
 extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias,
                                            int T, int H, int E, int topk, int32_t* ids, float* w, float* logits,
-                                           void* stream) {
+                                           int32_t* counter, void* stream) {
     EXL3B_CHECK(x_bf16 && wr_bf16 && ids && w && logits, "exl3b_router_topk: null pointer");
     EXL3B_CHECK(H % 256 == 0 && H <= 4096, "exl3b_router_topk: H must be a multiple of 256, <= 4096");
     EXL3B_CHECK(E >= 1 && E <= 1024, "exl3b_router_topk: 1 <= E <= 1024");
@@ -115,22 +141,18 @@ extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride,
     dim3 g1((E + 7) / 8, (T + TC - 1) / TC);
     const __nv_bfloat16* xp = (const __nv_bfloat16*)x_bf16;
     const __nv_bfloat16* wp = (const __nv_bfloat16*)wr_bf16;
+    int* ctr = (counter && T <= TC) ? counter : nullptr;   // fused selection when every token fits one block
+    cudaError_t e = cudaSuccess;
     switch (H / 32) {
-        case 8: router_logits_kernel<8, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 16: router_logits_kernel<16, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 24: router_logits_kernel<24, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 32: router_logits_kernel<32, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 40: router_logits_kernel<40, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 48: router_logits_kernel<48, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 56: router_logits_kernel<56, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 64: router_logits_kernel<64, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 80: router_logits_kernel<80, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 96: router_logits_kernel<96, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
-        case 128: router_logits_kernel<128, TC><<<g1, 256, 0, s>>>(xp, x_stride, wp, bias, T, H, E, logits); break;
+#define RL(CLV) case CLV: e = launch_k(router_logits_kernel<CLV, TC>, g1, dim3(256), 0, s, xp, x_stride, wp, bias, T, H, E, \
+                                       logits, topk, ids, w, ctr); break;
+        RL(8) RL(16) RL(24) RL(32) RL(40) RL(48) RL(56) RL(64) RL(80) RL(96) RL(128)
+#undef RL
         default: return exl3b_fail(EXL3B_EINVAL, "exl3b_router_topk: unsupported H");
     }
-    int rc = exl3b_launch_status("exl3b_router_topk(logits)");
-    if (rc) return rc;
-    router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, T, E, topk, ids, w);
-    return exl3b_launch_status("exl3b_router_topk(select)");
+    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    if (ctr) return 0;
+    e = launch_k(router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, (const float*)logits, T, E, topk, ids, w);
+    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    return 0;
 }

@@ -26,7 +26,7 @@ _SIGS = {
     "exl3b_blob_bytes": (i64, [ci, ci, ci, ci, ci]),
     "exl3b_dequant": (ci, [vp, ci, i64, ci, ci, ci, ci, vp, i64, vp]),
     "exl3b_blob_dequant": (ci, [vp, ci, ci, ci, ci, ci, ci, vp, vp]),
-    "exl3b_router_topk": (ci, [vp, i64, vp, vp, ci, ci, ci, ci, vp, vp, vp, vp]),
+    "exl3b_router_topk": (ci, [vp, i64, vp, vp, ci, ci, ci, ci, vp, vp, vp, vp, vp]),
     "exl3b_ensure": (ci, [vp, vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, ci, ci, vp, vp, vp, ci,
                           vp, vp, vp]),
     "exl3b_fill_copy": (ci, [vp, vp, vp, vp, i64, i64, ci, vp]),
@@ -35,6 +35,8 @@ _SIGS = {
     "exl3b_moe_decode_workspace": (i64, [ci, ci, ci, ci]),
     "exl3b_moe_decode": (ci, [vp, i64, ci, vp, vp, ci, ci, vp, vp, ci, ci, ci, ci, vp, i64, ci, vp, i64, ci, vp]),
     "exl3b_set_profile_events": (ci, [vp, vp, vp, vp]),
+    "exl3b_moe_decode_cached": (ci, [vp, i64, ci, vp, vp, ci, ci, ci, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, ci, ci,
+                                     vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, vp, i64, ci, vp, i64, ci, vp]),
     "exl3b_align_scratch": (i64, [ci, ci]),
     "exl3b_align": (ci, [vp, vp, ci, ci, ci, ci, vp, vp, ci, ci, vp, i64, vp]),
 }

@@ -217,12 +217,17 @@ class ExpertStore:
         return self.X.moe_forward(x, ids, w, self.ptrs(key) if ptrs is None else ptrs, self.I, self.K, self.E)
 
     def forward_cached(self, key, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor,
-                       max_fill: int | None = None) -> torch.Tensor:
+                       max_fill: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
         """Decode with the device-managed LRU cache: misses are copied from host into their LRU slot and the table is
         repointed within the call (no host sync, graph-safe).  With the tier on, picks in neither VRAM nor RAM are
         rewritten in place to (safe expert, weight 0) and logged to the miss ring."""
         ids, w = self._rt(topk_ids, topk_w)
         self._cache_used = True
+        if out is not None:   # extension: write into a caller buffer (same computation, no torch op dispatch)
+            return _ops._moe_forward_cached_impl(x, ids, w, self.ptrs_all, self.layer_index[key], self.slot_of_dev,
+                                                 self.slot_key, self.slot_last, self.tick, self.host_base, self.slot_base,
+                                                 self.fill_all, self.fill_list, self.E if max_fill is None else max_fill,
+                                                 self.I, self.K, self.E, self.pend, self.done_seq, out=out)
         return self.X.moe_forward_cached(x, ids, w, self.ptrs_all, self.layer_index[key], self.slot_of_dev,
                                          self.slot_key, self.slot_last, self.tick, self.host_base, self.slot_base,
                                          self.fill_all, self.fill_list, self.E if max_fill is None else max_fill,

@@ -95,8 +95,23 @@ def router_topk(x: torch.Tensor, wr: torch.Tensor, bias: torch.Tensor | None, to
     if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
         raise RuntimeError("exl3b200 router: bias must be contiguous fp32")
     check(_lib.lib().exl3b_router_topk(x.data_ptr(), x.stride(0), wr.data_ptr(), ptr(bias), T, H, E, topk,
-                                       ids.data_ptr(), w.data_ptr(), logits.data_ptr(), stream(x.device)), "router")
+                                       ids.data_ptr(), w.data_ptr(), logits.data_ptr(), _router_counter(x.device),
+                                       stream(x.device)), "router")
     return ids, w
+
+
+_ctr = {}
+
+
+def _router_counter(device) -> int:
+    """Per (device, stream) int32 arrival counter of the fused router selection.  Zeroed once; every launch leaves it
+    at zero.  Created on first use, so the first router call should come before any graph capture on that stream."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream(device))
+    t = _ctr.get(key)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=device)
+        _ctr[key] = t
+    return t.data_ptr()
 
 
 def dequant(words: torch.Tensor, rows16: int, row_stride: int, tile0: int, ntiles: int, K: int, planar: bool,
@@ -138,37 +153,42 @@ def _moe_forward_impl(x, topk_ids, topk_w, ptrs, I, K, n_experts):
 
 
 def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
-                             slot_base, fill_all, fill_list, max_fill, I, K, n_experts, pend, done_seq):
+                             slot_base, fill_all, fill_list, max_fill, I, K, n_experts, pend, done_seq, out=None):
     if ptrs_all.dtype != torch.int64 or fill_all.dtype != torch.int64 or slot_of.dtype != torch.int32:
         raise RuntimeError("exl3b200 moe_forward_cached: int64 ptrs_all / fill_all, int32 slot_of")
     E = n_experts
     M = x.shape[0]
     ptrs_l = ptrs_all.narrow(0, layer * E, E)
     if M == 0 or M >= G.prefill_min_m or slot_key.numel() == 0:
-        return _moe_forward_impl(x, topk_ids, topk_w, ptrs_l, I, K, E)
+        y = _moe_forward_impl(x, topk_ids, topk_w, ptrs_l, I, K, E)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
     if pend.numel() and done_seq.numel():
         raise RuntimeError("exl3b200 moe_forward_cached: copy-engine prefetch commits (pend/done_seq) not available")
     _check_route(topk_ids, topk_w)
+    _check_x(x)
     H = x.shape[1]
     blob = blob_bytes(H, I, K)
-    npairs = topk_ids.numel()
-    mf = min(max_fill, E)
-    vict = G.vict
-    ensure(topk_ids, topk_w, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob,
-           fill_all, fill_list, mf, vict=vict)
+    topk = topk_ids.shape[1] if topk_ids.dim() == 2 else 1
+    S = slot_key.numel()
+    if out is None:
+        out = torch.empty_like(x)
     L = _lib.lib()
-    s = stream(x.device)
-    nmax = min(mf, npairs)
-    fill_l = fill_all.narrow(0, layer * E, E)
-    if vict is not None and nmax > 0:
-        check(L.exl3b_victim_copy(vict.data_ptr(), host_base.data_ptr(), slot_base, blob, E, G.host_stride or blob,
-                                  ptr(G.ram_res), nmax, s), "victim_copy")
-    if nmax > 0:
-        check(L.exl3b_fill_copy(fill_list.data_ptr(), ptrs_l.data_ptr(), fill_l.data_ptr(), None, slot_base, blob,
-                                nmax, s), "fill_copy")
-    check(L.exl3b_commit(fill_list.data_ptr(), ptrs_l.data_ptr(), fill_l.data_ptr(), None, slot_base, blob, s),
-          "commit")
-    return moe_decode(x, topk_ids, topk_w, ptrs_l, I, K, E)
+    wsb = int(L.exl3b_moe_decode_workspace(M, topk, H, I))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
+    rr = G.ram_res
+    vict = G.vict
+    check(L.exl3b_moe_decode_cached(
+        x.data_ptr(), x.stride(0), int(x.dtype == torch.bfloat16), topk_ids.data_ptr(), topk_w.data_ptr(), M, topk, layer,
+        ptrs_all.data_ptr(), slot_of.data_ptr(), slot_key.data_ptr(), slot_last.data_ptr(), tick.data_ptr(),
+        host_base.data_ptr(), slot_base, blob, G.host_stride or blob, fill_all.data_ptr(), fill_list.data_ptr(),
+        min(max_fill, E), S, ptr(rr), ptr(G.ring if rr is not None else None),
+        (G.ring.numel() - 1) if rr is not None else 0, ptr(G.safe if rr is not None else None), ptr(vict), ptr(rr),
+        H, I, K, E, out.data_ptr(), out.stride(0), _OUT_CODE[out.dtype], ws.data_ptr(), wsb,
+        1 if G.skip_zero else 0, stream(x.device)), "moe_forward_cached")
+    return out
 
 
 def _moe_prefetch_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base, slot_base, pf_list,

@@ -51,7 +51,7 @@ def test_blob_bytes_and_abi():
                                  1 << 20, 2048, 1, 1 << 20, 1 << 30, 1, None),    # H % 128
     lambda L: L.exl3b_moe_decode(1 << 20, 2048, 1, 1 << 20, 1 << 20, 1, 10, 1 << 20, None, 2048, 768, 3, 512,
                                  1 << 20, 2048, 1, 1 << 20, 16, 1, None),          # workspace too small
-    lambda L: L.exl3b_router_topk(1 << 20, 2048, 1 << 20, None, 1, 2048, 512, 40, 1 << 20, 1 << 20, 1 << 20, None),
+    lambda L: L.exl3b_router_topk(1 << 20, 2048, 1 << 20, None, 1, 2048, 512, 40, 1 << 20, 1 << 20, 1 << 20, None, None),
     lambda L: L.exl3b_align(1 << 20, 1 << 20, 10, 10, 512, 32, 1 << 20, 1 << 20, 9, 10, 1 << 20, 1 << 20, None),
 ])
 def test_invalid_arguments_rejected_before_launch(call):
