@@ -113,6 +113,17 @@ int64_t exl3b_align_scratch(int P, int E);
 int exl3b_align(const int32_t* ids, const float* w, int P, int topk, int E, int pad, int32_t* ib, float* pair_w, int A,
                 int mxb, void* scratch, int64_t scratch_bytes, void* stream);
 
+/* Replaces moe_prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828 with GateUpDpasKernel :422-545, DownDpasKernel
+ * :548-635 and CombineKernel :371-395), the path moe_forward takes for M >= prefill_min_m (:1263-1314): the routed-MoE
+ * layer for many tokens as grouped tensor-core GEMMs (tcgen05, fp16 operands, fp32 accumulate in TMEM).  Arguments as
+ * exl3b_moe_decode; H % 256 == 0, I % 128 == 0.  Every pick's weighted output is stored fp16 and the combine sums
+ * those in fp32 in pick order, as the reference's prefill does.
+ * workspace: >= exl3b_moe_prefill_workspace(M, topk, H, I, E) bytes, 1024-byte aligned, owned by the caller. */
+int64_t exl3b_moe_prefill_workspace(int M, int topk, int H, int I, int E);
+int exl3b_moe_prefill(const void* x, int64_t x_stride, int x_bf16, const int32_t* ids, const float* w, int M, int topk,
+                      const int64_t* ptrs, const int32_t* kinfo, int H, int I, int K, int E, void* out,
+                      int64_t out_stride, int out_bf16, void* workspace, int64_t ws_bytes, int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -126,10 +126,17 @@ EXPORT int ora_tile_col(int t) { return (t >> 5) + 8 * ((t >> 2) & 1); }
  */
 EXPORT uint32_t ora_tile_state(const uint32_t* tw, int K, int t) {
     int nbits = 256 * K, end = (t + 1) * K;
+    int b0 = ((end - 16) % nbits + nbits) % nbits;   /* first bit of the window (circular) */
+    /* gather the 16 bits MSB-first: bits b0 .. b0+15 (mod nbits) */
     uint32_t st = 0;
-    for (int b = end - 16; b < end; ++b) {
-        int bb = ((b % nbits) + nbits) % nbits;
-        st = (st << 1) | ((tw[bb >> 5] >> (31 - (bb & 31))) & 1u);
+    int w = b0 >> 5, o = b0 & 31;
+    if (o <= 16 && b0 + 16 <= nbits) {
+        st = (tw[w] >> (16 - o)) & 0xFFFFu;                 /* window inside one word */
+    } else {
+        for (int b = 0; b < 16; ++b) {
+            int bb = (b0 + b) % nbits;
+            st = (st << 1) | ((tw[bb >> 5] >> (31 - (bb & 31))) & 1u);
+        }
     }
     return st;
 }
@@ -368,6 +375,88 @@ EXPORT void ora_moe_layer(const uint16_t* x, int x_is_bf16, const int32_t* ids, 
         }
     }
     free(y); free(acc); free(abuf); free(wg); free(wu); free(wd);
+}
+
+/*
+ * All picks of ONE expert (n picks: token rows x + tok[i] * x_stride, weights w[i]) -> y [n][H] fp32, with exactly
+ * expert_forward's arithmetic per pick: the weights are dequantised once and the GEMV sums run in the same ascending
+ * k order per output (k outer, outputs inner).  y_half = 1 rounds y to fp16 (the prefill's stored y, :626-631).
+ * Threads may call this concurrently for different experts.
+ */
+EXPORT void ora_expert_picks(const uint16_t* x, int64_t x_stride, int x_is_bf16, const int32_t* tok, const float* w,
+                             int n, const uint8_t* blob, int Kg, int Ku, int Kd, int H, int I, int y_half, float* y) {
+    OraGeom g = {H, I, Kg, Kg, Kd};
+    g.Ku = Ku;
+    uint16_t* wh = (uint16_t*)malloc((size_t)H * I * 2);
+    float* wg = (float*)malloc((size_t)H * I * 4);
+    float* wu = (float*)malloc((size_t)H * I * 4);
+    float* wd = (float*)malloc((size_t)H * I * 4);
+    ora_blob_dequant(blob, H, I, Kg, Ku, Kd, 0, wh);
+    for (size_t q = 0; q < (size_t)H * I; ++q) wg[q] = ora_f16_to_f32(wh[q]);
+    ora_blob_dequant(blob, H, I, Kg, Ku, Kd, 1, wh);
+    for (size_t q = 0; q < (size_t)H * I; ++q) wu[q] = ora_f16_to_f32(wh[q]);
+    ora_blob_dequant(blob, H, I, Kg, Ku, Kd, 2, wh);
+    for (size_t q = 0; q < (size_t)H * I; ++q) wd[q] = ora_f16_to_f32(wh[q]);
+    uint16_t* xg = (uint16_t*)malloc((size_t)H * 2);
+    uint16_t* xu = (uint16_t*)malloc((size_t)H * 2);
+    uint16_t* abuf = (uint16_t*)malloc((size_t)I * 2);
+    double* sg = (double*)malloc((size_t)I * 8);
+    double* su = (double*)malloc((size_t)I * 8);
+    double* sd = (double*)malloc((size_t)H * 8);
+    float* gg = (float*)malloc((size_t)I * 4);
+    float* uu = (float*)malloc((size_t)I * 4);
+    float* vv = (float*)malloc((size_t)H * 4);
+    const uint16_t* svg = vec_ptr(blob, &g, 2);
+    const uint16_t* svu = vec_ptr(blob, &g, 3);
+    const uint16_t* sud = vec_ptr(blob, &g, 4);
+    const uint16_t* svd = vec_ptr(blob, &g, 5);
+    for (int p = 0; p < n; ++p) {
+        const uint16_t* xr = x + (size_t)tok[p] * x_stride;
+        ora_had_in(xr, x_is_bf16, vec_ptr(blob, &g, 0), H, xg);
+        ora_had_in(xr, x_is_bf16, vec_ptr(blob, &g, 1), H, xu);
+        for (int c = 0; c < I; ++c) { sg[c] = 0.0; su[c] = 0.0; }
+        for (int k = 0; k < H; ++k) {
+            const double a = (double)ora_f16_to_f32(xg[k]), b = (double)ora_f16_to_f32(xu[k]);
+            const float* rg = wg + (size_t)k * I;
+            const float* ru = wu + (size_t)k * I;
+            for (int c = 0; c < I; ++c) { sg[c] += a * (double)rg[c]; su[c] += b * (double)ru[c]; }
+        }
+        for (int c = 0; c < I; ++c) { gg[c] = (float)sg[c]; uu[c] = (float)su[c]; }
+        for (int nb = 0; nb < I / 128; ++nb) {
+            float* gb = gg + nb * 128;
+            float* ub = uu + nb * 128;
+            float act[128];
+            ora_fwht128(gb);
+            ora_fwht128(ub);
+            for (int i = 0; i < 128; ++i) {
+                float gv = rn16(gb[i] * kRsqrt128 * ora_f16_to_f32(svg[nb * 128 + i]));
+                float uv = rn16(ub[i] * kRsqrt128 * ora_f16_to_f32(svu[nb * 128 + i]));
+                float a = gv / (1.0f + expf(-gv)) * uv;
+                a = rn16(a);
+                act[i] = rn16(a * ora_f16_to_f32(sud[nb * 128 + i]));
+            }
+            ora_fwht128(act);
+            for (int i = 0; i < 128; ++i) abuf[nb * 128 + i] = ora_f32_to_f16(act[i] * kRsqrt128);
+        }
+        for (int c = 0; c < H; ++c) sd[c] = 0.0;
+        for (int k = 0; k < I; ++k) {
+            const double a = (double)ora_f16_to_f32(abuf[k]);
+            const float* rd = wd + (size_t)k * H;
+            for (int c = 0; c < H; ++c) sd[c] += a * (double)rd[c];
+        }
+        for (int c = 0; c < H; ++c) vv[c] = (float)sd[c];
+        float* yp = y + (size_t)p * H;
+        for (int nb = 0; nb < H / 128; ++nb) {
+            float* vb = vv + nb * 128;
+            ora_fwht128(vb);
+            for (int i = 0; i < 128; ++i) {
+                float v = vb[i] * (kRsqrt128 * w[p]) * ora_f16_to_f32(svd[nb * 128 + i]);
+                yp[nb * 128 + i] = y_half ? ora_f16_to_f32(ora_f32_to_f16(v)) : v;
+            }
+        }
+    }
+    free(wh); free(wg); free(wu); free(wd); free(xg); free(xu); free(abuf);
+    free(sg); free(su); free(sd); free(gg); free(uu); free(vv);
 }
 
 /*

@@ -62,6 +62,7 @@ def lib():
             "ora_had_in": (None, [u16p, ci, u16p, ci, u16p]),
             "ora_moe_layer": (None, [u16p, ci, i32p, f32p, ci, ci, vp, vp, ci, ci, ci, ci, vp, vp, vp]),
             "ora_dense_glu": (None, [u16p, ci, vp, ci, ci, ci, ci, ci, f32p]),
+            "ora_expert_picks": (None, [u16p, ctypes.c_int64, ci, i32p, f32p, ci, vp, ci, ci, ci, ci, ci, ci, f32p]),
             "ora_router_dot": (ctypes.c_float, [u16p, u16p, ci]),
             "ora_router": (None, [u16p, u16p, vp, ci, ci, ci, ci, i32p, f32p, vp]),
             "ora_align": (None, [i32p, f32p, ci, ci, ci, ci, i32p, i32p, i32p, i32p, i32p, i32p, f32p, i32p, vp, vp]),
@@ -157,6 +158,53 @@ def moe_layer(x_bits: np.ndarray, ids: np.ndarray, w: np.ndarray, blobs: list, H
     lib().ora_moe_layer(x_bits, int(x_is_bf16), ids, w, M, topk, ctypes.cast(arr, ctypes.c_void_p), _ptr(ki),
                         H, I, K, 2 if out_f32 else 1, _ptr(out), _ptr(y), _ptr(ab))
     return (out, y, ab) if want_y else out
+
+
+def moe_layer_fast(x_bits: np.ndarray, ids: np.ndarray, w: np.ndarray, blobs: list, H: int, I: int, K: int = 3,
+                   kinfo: np.ndarray | None = None, x_is_bf16: bool = True, out_f32: bool = False,
+                   threads: int | None = None, y_half: bool = False, rows: np.ndarray | None = None):
+    """moe_layer grouped by expert: each expert's weights are dequantised once and all of its picks run on one thread
+    (experts on parallel threads; the C code releases the GIL).  Same per-pick arithmetic and the same outputs as
+    moe_layer (the combine adds the picks in k order in fp32).  y_half=True gives the prefill semantics: every pick's
+    weighted output is rounded to fp16 before the combine (the reference's moe_prefill stores y as fp16).  rows: only
+    these token rows are computed (returned in that order)."""
+    import concurrent.futures as cf
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows = np.arange(ids.shape[0]) if rows is None else np.asarray(rows)
+    sid, sw = ids[rows], w[rows]
+    M, topk = sid.shape
+    flat_e = sid.ravel()
+    flat_t = np.repeat(rows.astype(np.int32), topk)
+    flat_w = sw.ravel()
+    y = np.zeros((M * topk, H), dtype=np.float32)
+    L = lib()
+    experts = np.unique(flat_e)
+
+    def run(e):
+        sel = np.nonzero(flat_e == e)[0]
+        tok = np.ascontiguousarray(flat_t[sel])
+        we = np.ascontiguousarray(flat_w[sel])
+        ye = np.empty((len(sel), H), dtype=np.float32)
+        kg = ku = kd = K
+        if kinfo is not None:
+            v = int(kinfo[e]); kg, ku, kd = v & 15, (v >> 4) & 15, (v >> 8) & 15
+        b = np.ascontiguousarray(blobs[e], dtype=np.uint8)
+        L.ora_expert_picks(x_bits, H if x_bits.ndim == 1 else x_bits.shape[1], int(x_is_bf16), tok, we, len(sel),
+                           b.ctypes.data, kg, ku, kd, H, I, int(y_half), ye)
+        y[sel] = ye
+
+    with cf.ThreadPoolExecutor(threads or (os.cpu_count() or 1)) as ex:
+        list(ex.map(run, experts))
+    y = y.reshape(M, topk, H)
+    acc = np.zeros((M, H), dtype=np.float32)
+    for k in range(topk):
+        acc += y[:, k]
+    if out_f32:
+        return acc
+    u = acc.view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16) if x_is_bf16 else acc.astype(np.float16).view(np.uint16)
 
 
 def dense_glu(x_bits: np.ndarray, blob: np.ndarray, H: int, I: int, Kg: int, Ku: int, Kd: int) -> np.ndarray:

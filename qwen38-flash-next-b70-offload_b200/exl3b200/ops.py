@@ -81,6 +81,31 @@ def moe_decode(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, ptrs: torch.
     return out
 
 
+def moe_prefill(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, ptrs: torch.Tensor, I: int, K: int, E: int,
+                kinfo: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed MoE through the grouped tensor-core prefill kernels (the reference's moe_prefill): H % 256 == 0,
+    I % 128 == 0; sized for many tokens."""
+    _check_x(x)
+    _check_route(ids, w)
+    if ptrs.dtype != torch.int64 or not ptrs.is_contiguous():
+        raise RuntimeError("exl3b200: ptrs must be contiguous int64")
+    M, H = x.shape
+    topk = ids.shape[1] if ids.dim() == 2 else 1
+    if out is None:
+        out = torch.empty_like(x)
+    if M == 0:
+        return out
+    L = _lib.lib()
+    wsb = int(L.exl3b_moe_prefill_workspace(M, topk, H, I, E))
+    raw = torch.empty(wsb + 1024, dtype=torch.uint8, device=x.device)
+    base = (raw.data_ptr() + 1023) & ~1023
+    check(L.exl3b_moe_prefill(x.data_ptr(), x.stride(0), int(x.dtype == torch.bfloat16), ids.data_ptr(), w.data_ptr(),
+                              M, topk, ptrs.data_ptr(), ptr(kinfo), H, I, K, E, out.data_ptr(), out.stride(0),
+                              _OUT_CODE[out.dtype], base, wsb, 0, stream(x.device)),
+          "moe_prefill")
+    return out
+
+
 def router_topk(x: torch.Tensor, wr: torch.Tensor, bias: torch.Tensor | None, topk: int):
     """Router GEMV + softmax top-k: returns (ids int32 [T, topk], w fp32 [T, topk])."""
     if x.dtype != torch.bfloat16 or wr.dtype != torch.bfloat16:
@@ -147,9 +172,19 @@ def ensure(ids, w, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_
 
 # ------------------------------------------------------------------------------------------------ reference ops
 def _moe_forward_impl(x, topk_ids, topk_w, ptrs, I, K, n_experts):
+    """moe_forward (exl3_moe.a8.sycl:1263-1314): M >= prefill_min_m takes the prefill GEMMs, else the decode kernels."""
     if x.shape[0] == 0:
         return torch.empty_like(x)
+    if x.shape[0] >= G.prefill_min_m and x.shape[1] % 256 == 0:
+        return moe_prefill(x, topk_ids, topk_w, ptrs, I, K, n_experts)
     return moe_decode(x, topk_ids, topk_w, ptrs, I, K, n_experts)
+
+
+def _moe_forward_mixed_impl(x, topk_ids, topk_w, ptrs, kinfo, I, n_experts):
+    """Per-expert K (kinfo: Kg | Ku << 4 | Kd << 8); same decode / prefill split as moe_forward."""
+    if x.shape[0] >= G.prefill_min_m and x.shape[1] % 256 == 0:
+        return moe_prefill(x, topk_ids, topk_w, ptrs, I, 0, n_experts, kinfo=kinfo)
+    return moe_decode(x, topk_ids, topk_w, ptrs, I, 0, n_experts, kinfo=kinfo)
 
 
 def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
@@ -342,8 +377,7 @@ def register() -> None:
     lib.impl("moe_prefetch", _moe_prefetch_impl, "CUDA")
     lib.impl("moe_align", _moe_align_impl, "CUDA")
     lib.impl("router_topk", lambda x, wr, bias, topk: router_topk(x, wr, bias, topk), "CUDA")
-    lib.impl("moe_forward_mixed",
-             lambda x, ids, w, ptrs, kinfo, I, E: moe_decode(x, ids, w, ptrs, I, 0, E, kinfo=kinfo), "CUDA")
+    lib.impl("moe_forward_mixed", _moe_forward_mixed_impl, "CUDA")
 
     torch.library.register_fake(f"{NS}::moe_forward", lambda x, *a: torch.empty_like(x), lib=lib)
     torch.library.register_fake(f"{NS}::moe_forward_cached", lambda x, *a: torch.empty_like(x), lib=lib)
