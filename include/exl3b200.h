@@ -113,6 +113,16 @@ int64_t exl3b_align_scratch(int P, int E);
 int exl3b_align(const int32_t* ids, const float* w, int P, int topk, int E, int pad, int32_t* ib, float* pair_w, int A,
                 int mxb, void* scratch, int64_t scratch_bytes, void* stream);
 
+/* No counterpart in the reference.  exl3b_moe_decode for callers that cannot allocate device memory: the same
+ * kernels and arguments without workspace / ws_bytes; the scratch is a fixed 8 MiB device array of the library
+ * (exl3b_moe_decode_workspace(M, topk, H, I) must be <= 8 MiB: up to 5 tokens at top-10 with H = 2048, I = 768; larger
+ * calls return EXL3B_EINVAL).  The first call on each device looks the array's address up, so make it before any
+ * stream capture on that device.  Nothing has to be zeroed by the caller.  One scratch per device: calls that overlap
+ * on one device race; order them on one stream or with events. */
+int exl3b_moe_decode_noalloc(const void* x, int64_t x_stride, int x_bf16, const int32_t* ids, const float* w, int M,
+                             int topk, const int64_t* ptrs, const int32_t* kinfo, int H, int I, int K, int E, void* out,
+                             int64_t out_stride, int out_bf16, int flags, void* stream);
+
 /* Replaces moe_prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828 with GateUpDpasKernel :422-545, DownDpasKernel
  * :548-635 and CombineKernel :371-395), the path moe_forward takes for M >= prefill_min_m (:1263-1314): the routed-MoE
  * layer for many tokens as grouped tensor-core GEMMs (tcgen05, fp16 operands, fp32 accumulate in TMEM).  Arguments as
