@@ -4,28 +4,34 @@
 // Pipeline (all on the caller's stream):
 //   align    (exl3b_align.cu): picks sorted by expert, stable;
 //   tiles    : 256-row tiles per active expert (a | m-pair << 16);
-//   had_in   : xh[p][proj][H] = fp16(FWHT(fp16(x[tok] * suh)) r) per sorted pick p and projection (:462-475);
-//   gate-up  : CTA per (tile, 128-column block of I): D_g, D_u [<=256 rows x 128] in TMEM (512 columns);
-//              B operands (gate / up W_inner) decoded from the trellis by all 8 warps straight into 128-byte-swizzled
-//              shared memory, A operands (xh rows) by cp.async, one thread issues tcgen05.mma (kind::f16, fp32 accumulate),
-//              double-buffered against tcgen05.commit mbarriers; epilogue per row from tcgen05.ld: FWHT, svh, SwiGLU,
-//              suh_d, FWHT -> abuf[p][I] (fp16, the reference's :531-541);
-//   down     : CTA per (tile, 256-column block of H): D [<=256 x 256] in TMEM; epilogue FWHT * r * w * svh_d -> y[p][H]
-//              stored fp16 as the reference's prefill does (:626-631, :802);
+//   had_in   : xh[proj][p][H] = fp16(FWHT(fp16(x[tok] * suh)) r) per sorted pick p and projection (:462-475), one warp
+//              per pick;
+//   gate-up  : CTA per (tile, 128-column block of I), warp-specialised:
+//                warp 9 (one lane) streams the A operand (xh rows, 64-k chunks) with TMA into 128-byte-swizzled
+//                shared memory; warps 0-7 decode the B operands (gate / up W_inner, 16x16 trellis tiles) in registers
+//                and store them with stmatrix into the same swizzled layout; warp 8 (one lane) issues tcgen05.mma
+//                (kind::f16, fp32 accumulate) into TMEM: D_g, D_u [<= 256 rows x 128] (512 columns).  Stages are
+//                handed over with mbarriers (TMA bytes, decoder arrivals, tcgen05.commit);
+//              epilogue per row from tcgen05.ld: FWHT, svh, SwiGLU, suh_d, FWHT -> abuf[p][I] (fp16, :531-541);
+//   down     : same structure, CTA per (tile, 256-column block of H): D [<= 256 x 256]; epilogue FWHT * r * w * svh_d
+//              -> y[p][H] stored fp16 as the reference's prefill does (:626-631, :802);
 //   combine  : out[t] = sum_k y[pair_of[t, k]] in fixed k order (fp32), rounded to the output type.
-// Weight decode is once per (expert, column block, 256-row tile); rows past an expert's count are computed on
-// whatever rows follow in the buffers and never stored.
+// Weights are decoded once per (expert, column block, 256-row tile); rows past an expert's count are computed on
+// whatever rows follow in the buffers and never stored.  Every wait is bounded (exl3b_tc.cuh mbar_wait).
 #include "exl3b_common.cuh"
 #include "exl3b_capi_util.h"
 #include "exl3b_launch.h"
 #include "exl3b_tc.cuh"
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <algorithm>
+#include <mutex>
 
 namespace exl3b {
 
 struct PrefillArgs {
     const void* x; long long xs; int x_bf16;
-    int M, topk, P;
+    int M, topk, P, Prow;
     const int64_t* ptrs; const int32_t* kinfo;
     int H, I, K, E;
     void* out; long long os; int out_bf16;
@@ -68,7 +74,157 @@ __global__ void __launch_bounds__(1024) tiles_kernel(PrefillArgs p) {
 }
 
 // ------------------------------------------------------------------------------------------------ had_in
-// One thread per (sorted pick p, projection, 128-block kb): the 128 values stay in registers for the FWHT.
+// One warp per sorted pick: the token row is read once for both projections; each 128-block is held as 4 values per
+// lane and transformed with the in-warp FWHT (same butterfly order as the reference).
+__global__ void __launch_bounds__(256) had_in_kernel(PrefillArgs p) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const long long prl = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (prl >= p.P) return;
+    const int pr = (int)prl;
+    const int na = *p.n_act;
+    int lo = 0, hi = na - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (p.act_start[mid] <= pr) lo = mid; else hi = mid - 1;
+    }
+    const int e = p.act_expert[lo];
+    int kg, ku, kd;
+    expert_kv(p, e, kg, ku, kd);
+    const Geom gm{p.H, p.I, kg, ku, kd};
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(p.ptrs[e]);
+    const int tok = p.pair_tok[pr];
+    const uint16_t* xr = reinterpret_cast<const uint16_t*>(p.x) + (size_t)tok * p.xs;
+#pragma unroll 1
+    for (int proj = 0; proj < 2; ++proj) {
+        const __half* suh = reinterpret_cast<const __half*>(blob + gm.off_suh_g() + (size_t)proj * p.H * 2);
+        __half* dst = p.xh + ((size_t)proj * p.Prow + pr) * p.H;
+#pragma unroll 2
+        for (int kb = 0; kb < p.H / 128; ++kb) {
+            const int i0 = kb * 128 + lane * 4;
+            uint2 xv = *reinterpret_cast<const uint2*>(xr + i0);
+            uint2 sv = __ldg(reinterpret_cast<const uint2*>(suh + i0));
+            float xf[4];
+            if (p.x_bf16) {
+                xf[0] = __uint_as_float(xv.x << 16); xf[1] = __uint_as_float(xv.x & 0xFFFF0000u);
+                xf[2] = __uint_as_float(xv.y << 16); xf[3] = __uint_as_float(xv.y & 0xFFFF0000u);
+            } else {
+                __half2 h0 = *reinterpret_cast<__half2*>(&xv.x), h1 = *reinterpret_cast<__half2*>(&xv.y);
+                xf[0] = __low2float(h0); xf[1] = __high2float(h0); xf[2] = __low2float(h1); xf[3] = __high2float(h1);
+            }
+            __half2 s0 = *reinterpret_cast<__half2*>(&sv.x), s1 = *reinterpret_cast<__half2*>(&sv.y);
+            float v[4] = {rn16(xf[0] * __low2float(s0)), rn16(xf[1] * __high2float(s0)), rn16(xf[2] * __low2float(s1)),
+                          rn16(xf[3] * __high2float(s1))};
+            fwht128_warp(v, lane);
+            __half2 o0 = __floats2half2_rn(v[0] * kRsqrt128, v[1] * kRsqrt128);
+            __half2 o1 = __floats2half2_rn(v[2] * kRsqrt128, v[3] * kRsqrt128);
+            uint2 o;
+            o.x = *reinterpret_cast<uint32_t*>(&o0);
+            o.y = *reinterpret_cast<uint32_t*>(&o1);
+            *reinterpret_cast<uint2*>(dst + i0) = o;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ grouped GEMM
+// Shared memory per stage: PHASE 0 (gate-up): A[proj][mt] 4 x 16 KB (128 rows x 64 fp16, SW128), B[proj] 2 x 16 KB
+// (128 columns x 64 fp16); PHASE 1 (down): A[mt] 2 x 16 KB, B 32 KB (256 columns x 64 fp16).  After the stages: the
+// mbarriers, the TMEM base slot and the epilogue vectors.
+template <int PHASE>
+struct GemmCfg {
+    static constexpr int NST = PHASE == 0 ? 2 : 3;
+    static constexpr int A_BYTES = PHASE == 0 ? 4 * 16384 : 2 * 16384;
+    static constexpr int B_BYTES = 32768;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int SMEM = 1024 + NST * STAGE + 1024;
+    static constexpr int THREADS = 320;   // warps 0-7 decode + epilogue, warp 8 MMA + TMEM, warp 9 TMA
+};
+
+struct DecCtx {
+    const uint32_t* wbase;   // first word of this warp's projection region (row 0)
+    size_t row_words;        // words per tile row
+    int ctg;                 // first global column tile of the warp's 2 tiles
+    uint32_t sboff;          // byte offset of the warp's first tile inside a stage's B region
+};
+
+// Decoder warp: 2 column tiles x 4 tile rows (64 k) per chunk; words prefetched one chunk ahead in registers.
+template <int K, int PHASE>
+__device__ __forceinline__ void decode_loop(const DecCtx& d, uint8_t* sbase, uint64_t* full_b, uint64_t* empty,
+                                            int nchunks) {
+    using C = GemmCfg<PHASE>;
+    constexpr int W = Geo<K>::W, G = Geo<K>::G;
+    const int lane = threadIdx.x & 31;
+    LaneWin<K> lw;
+    lw.init(lane, true);
+    const int nl = (lane & 7) + 8 * ((lane >> 3) & 1), kc = (lane >> 4) & 1;
+    uint32_t soff[4];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) soff[rr] = (uint32_t)nl * 128u + ((uint32_t)((2 * rr + kc) ^ (lane & 7)) << 4);
+    const uint32_t* gp0 = d.wbase + (size_t)(d.ctg >> 2) * 4 * W + (d.ctg & 3) * G;
+    const uint32_t* gp1 = d.wbase + (size_t)((d.ctg + 1) >> 2) * 4 * W + ((d.ctg + 1) & 3) * G;
+    uint32_t wa[8], wb[8], wc[8];
+    auto load = [&](int c) {
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t* gp = (j ? gp1 : gp0) + (size_t)(c * 4 + rr) * d.row_words;
+                wa[rr * 2 + j] = __ldg(gp + lw.oA);
+                wb[rr * 2 + j] = __ldg(gp + lw.oB);
+                wc[rr * 2 + j] = LaneWin<K>::kNeedC ? __ldg(gp + lw.oC) : 0u;
+            }
+    };
+    load(0);
+    const uint32_t s0 = smem_u32(sbase) + C::A_BYTES + d.sboff;
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c % C::NST;
+        uint32_t ca[8], cb[8], cc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { ca[i] = wa[i]; cb[i] = wb[i]; cc[i] = wc[i]; }
+        if (c + 1 < nchunks) load(c + 1);
+        if (c >= C::NST) mbar_wait(&empty[s], (uint32_t)((c / C::NST) - 1) & 1u);
+        const uint32_t sb = s0 + (uint32_t)s * C::STAGE;
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                uint32_t f[4];
+                decode8<K>(ca[rr * 2 + j], cb[rr * 2 + j], cc[rr * 2 + j], lw.p0, f);
+                stmatrix_x4(sb + (uint32_t)j * 2048u + soff[rr], f[0], f[1], f[2], f[3]);
+            }
+        fence_async_smem();
+        mbar_arrive(&full_b[s]);
+    }
+}
+
+template <int PHASE>
+__device__ __forceinline__ void decode_loop_any(int K, const DecCtx& d, uint8_t* sbase, uint64_t* full_b,
+                                                uint64_t* empty, int nchunks) {
+    switch (K) {
+        case 2: decode_loop<2, PHASE>(d, sbase, full_b, empty, nchunks); break;
+        case 3: decode_loop<3, PHASE>(d, sbase, full_b, empty, nchunks); break;
+        case 4: decode_loop<4, PHASE>(d, sbase, full_b, empty, nchunks); break;
+        case 5: decode_loop<5, PHASE>(d, sbase, full_b, empty, nchunks); break;
+        default:
+            // unsupported K (already flagged kErrGeometry): no decode, but the stage hand-over still runs so that
+            // no other role of the CTA waits on these warps
+            for (int c = 0; c < nchunks; ++c) {
+                const int s = c % GemmCfg<PHASE>::NST;
+                if (c >= GemmCfg<PHASE>::NST) mbar_wait(&empty[s], (uint32_t)((c / GemmCfg<PHASE>::NST) - 1) & 1u);
+                mbar_arrive(&full_b[s]);
+            }
+            break;
+    }
+}
+
+// Epilogue helper: the thread owns TMEM lane (row) 32*(wid%4) + lane of M-tile mt = wid / 4.
+__device__ __forceinline__ void tmem_row128(uint32_t taddr, float v[128]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tmem_ld32(taddr + q * 32, v + q * 32);
+}
+
 __device__ __forceinline__ void fwht128_regs(float v[128]) {
 #pragma unroll
     for (int h = 1; h < 128; h <<= 1)
@@ -82,194 +238,95 @@ __device__ __forceinline__ void fwht128_regs(float v[128]) {
             }
 }
 
-__global__ void __launch_bounds__(128) had_in_kernel(PrefillArgs p) {
+template <int PHASE>
+// One CTA per SM (TMEM 512 columns, ~194 KB shared memory).  10 warps put 3 warps on two of the four SM
+// sub-partitions, whose register files hold 16,384 registers each: at most 168 registers per thread.
+__global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, const __grid_constant__ CUtensorMap tmA) {
+    using C = GemmCfg<PHASE>;
+    constexpr int NST = C::NST;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* tail = sbase + NST * C::STAGE;
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(tail);
+    uint64_t* full_b = full_a + NST;
+    uint64_t* empty = full_b + NST;
+    uint64_t* done = empty + NST;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tail + 128);
+    __half* vec = reinterpret_cast<__half*>(tail + 256);   // epilogue vectors (3 x 128 or 256 fp16)
+    const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
     pdl_wait();
     pdl_trigger();
-    const int nkb = p.H / 128;
-    const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (long long)p.P * 2 * nkb) return;
-    const int kb = (int)(gid % nkb);
-    const int proj = (int)((gid / nkb) & 1);
-    const int pr = (int)(gid / (2 * nkb));
-    // active expert of pick pr: last a with act_start[a] <= pr
-    const int na = *p.n_act;
-    int lo = 0, hi = na - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (p.act_start[mid] <= pr) lo = mid; else hi = mid - 1;
-    }
-    const int e = p.act_expert[lo];
+    const int NB = PHASE == 0 ? p.I / 128 : p.H / 256;
+    const int n_tiles = *p.n_tiles;
+    const int b = blockIdx.x;
+    if (b >= n_tiles * NB) return;
+    const int tv = p.tiles[b / NB], nb = b % NB;
+    const int a = tv & 0xFFFF, mp = tv >> 16;
+    const int e = p.act_expert[a], cnt = p.act_cnt[a];
+    const int row0 = p.act_start[a] + mp * 256;
+    const int rows = min(256, cnt - mp * 256);
+    const int nmt = rows > 128 ? 2 : 1;
     int kg, ku, kd;
     expert_kv(p, e, kg, ku, kd);
     const Geom gm{p.H, p.I, kg, ku, kd};
-    const uint8_t* blob = reinterpret_cast<const uint8_t*>(p.ptrs[e]);
-    const uint4* sp = reinterpret_cast<const uint4*>(blob + gm.off_suh_g() + (size_t)proj * p.H * 2 + (size_t)kb * 256);
-    const int tok = p.pair_tok[pr];
-    const uint4* xp = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.x) + ((size_t)tok * p.xs + (size_t)kb * 128) * 2);
-    float v[128];
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        uint4 xv = __ldg(xp + q), sv = __ldg(sp + q);
-        const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
-        const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float x0, x1;
-            if (p.x_bf16) { x0 = __uint_as_float(xw[j] << 16); x1 = __uint_as_float(xw[j] & 0xFFFF0000u); }
-            else { __half2 h = *reinterpret_cast<const __half2*>(&xw[j]); x0 = __low2float(h); x1 = __high2float(h); }
-            __half2 s = *reinterpret_cast<const __half2*>(&sw[j]);
-            v[q * 8 + 2 * j] = rn16(x0 * __low2float(s));
-            v[q * 8 + 2 * j + 1] = rn16(x1 * __high2float(s));
-        }
-    }
-    fwht128_regs(v);
-    uint4* op = reinterpret_cast<uint4*>(p.xh + ((size_t)pr * 2 + proj) * p.H + (size_t)kb * 128);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        uint4 o;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __half2 h = __floats2half2_rn(v[q * 8 + 2 * j] * kRsqrt128, v[q * 8 + 2 * j + 1] * kRsqrt128);
-            ow[j] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        op[q] = o;
-    }
-}
-
-// ------------------------------------------------------------------------------------------------ grouped GEMM
-// Shared memory per stage: PHASE 0 (gate-up): A[proj][mt] 4 x 16 KB (128 rows x 64 fp16, SW128), B[proj] 2 x 16 KB
-// (128 columns x 64 fp16); PHASE 1 (down): A[mt] 2 x 16 KB, B 32 KB (256 columns x 64 fp16).
-template <int PHASE>
-struct GemmCfg {
-    static constexpr int A_BYTES = PHASE == 0 ? 4 * 16384 : 2 * 16384;
-    static constexpr int B_BYTES = 32768;
-    static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int SMEM = 1024 + 2 * STAGE + 1024;   // alignment slack + 2 stages + barriers / vectors
-};
-
-// Per-warp B-operand work of one K-chunk (64 k = 4 tile rows x this warp's 2 column tiles): the trellis words of the
-// chunk are prefetched into registers one chunk ahead, then decoded into the 128-byte-swizzled B tile.
-struct BWork {
-    const uint32_t* wbase;   // first word of this warp's projection region
-    size_t row_words;        // words per tile row
-    int ctg, ctl;            // first column tile (within the projection / within the CTA's B tile)
-    uint32_t wa[8], wb[8], wc[8];
-};
-
-template <int K>
-__device__ __forceinline__ void bwork_load(BWork& bw, int c) {
-    constexpr int W = Geo<K>::W, G = Geo<K>::G;
-    LaneWin<K> lw;
-    lw.init(threadIdx.x & 31, true);
-#pragma unroll
-    for (int rr = 0; rr < 4; ++rr)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            int ct = bw.ctg + j;
-            const uint32_t* gp = bw.wbase + (size_t)(c * 4 + rr) * bw.row_words + (size_t)(ct >> 2) * 4 * W + (ct & 3) * G;
-            bw.wa[rr * 2 + j] = __ldg(gp + lw.oA);
-            bw.wb[rr * 2 + j] = __ldg(gp + lw.oB);
-            bw.wc[rr * 2 + j] = LaneWin<K>::kNeedC ? __ldg(gp + lw.oC) : 0u;
-        }
-}
-
-template <int K>
-__device__ __forceinline__ void bwork_decode(BWork& bw, int c, int nchunks, uint8_t* sBp) {
-    const int lane = threadIdx.x & 31;
-    LaneWin<K> lw;
-    lw.init(lane, true);
-    uint32_t ca[8], cb[8], cc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { ca[i] = bw.wa[i]; cb[i] = bw.wb[i]; cc[i] = bw.wc[i]; }
-    if (c + 1 < nchunks) bwork_load<K>(bw, c + 1);
-#pragma unroll
-    for (int rr = 0; rr < 4; ++rr)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            uint32_t f[4];
-            decode8<K>(ca[rr * 2 + j], cb[rr * 2 + j], cc[rr * 2 + j], lw.p0, f);
-            const int n0 = (bw.ctl + j) * 16 + (lane >> 2);
-            const int k0 = rr * 16 + 2 * (lane & 3);
-            *reinterpret_cast<uint32_t*>(sBp + sw128_off(n0, k0)) = f[0];
-            *reinterpret_cast<uint32_t*>(sBp + sw128_off(n0, k0 + 8)) = f[2];
-            *reinterpret_cast<uint32_t*>(sBp + sw128_off(n0 + 8, k0)) = f[1];
-            *reinterpret_cast<uint32_t*>(sBp + sw128_off(n0 + 8, k0 + 8)) = f[3];
-        }
-}
-
-__device__ __forceinline__ void bwork_load_any(int K, BWork& bw, int c) {
-    switch (K) {
-        case 2: bwork_load<2>(bw, c); break;
-        case 3: bwork_load<3>(bw, c); break;
-        case 4: bwork_load<4>(bw, c); break;
-        case 5: bwork_load<5>(bw, c); break;
-        default: break;
-    }
-}
-__device__ __forceinline__ void bwork_decode_any(int K, BWork& bw, int c, int nchunks, uint8_t* sBp) {
-    switch (K) {
-        case 2: bwork_decode<2>(bw, c, nchunks, sBp); break;
-        case 3: bwork_decode<3>(bw, c, nchunks, sBp); break;
-        case 4: bwork_decode<4>(bw, c, nchunks, sBp); break;
-        case 5: bwork_decode<5>(bw, c, nchunks, sBp); break;
-        default: break;
-    }
-}
-
-// K loop of one CTA: A by cp.async, B by decode, one thread issues the chunk's MMAs and commits them to the stage's
-// mbarrier; a stage is rewritten only after the commit of the MMAs that read it (two chunks earlier).
-template <int PHASE>
-__device__ __forceinline__ void gemm_mainloop(const PrefillArgs& p, uint8_t* sbase, uint64_t* mbar, uint32_t tbase,
-                                              int e, int row0, int rows, int nb, const Geom& gm, int Kw) {
-    using C = GemmCfg<PHASE>;
-    const int tid = threadIdx.x, wid = tid >> 5;
     const int KD = PHASE == 0 ? p.H : p.I;
     const int nchunks = KD / 64;
-    const int nmt = rows > 128 ? 2 : 1;
-    const uint32_t* words = reinterpret_cast<const uint32_t*>(p.ptrs[e]);
-    const int pj = PHASE == 0 ? (wid >> 2) : 0;
-    BWork bw;
-    bw.ctl = PHASE == 0 ? (wid & 3) * 2 : wid * 2;
-    bw.ctg = PHASE == 0 ? nb * 8 + bw.ctl : nb * 16 + bw.ctl;
-    bw.row_words = PHASE == 0 ? gm.gu_row_words() : gm.d_row_words();
-    bw.wbase = words + (PHASE == 0 ? (pj ? (size_t)(gm.I / 16) * 8 * gm.Kg : 0) : gm.gu_words());
-    bwork_load_any(Kw, bw, 0);
-    uint32_t parity[2] = {0u, 0u};
-    const uint32_t idesc = idesc_f16(128, PHASE == 0 ? 128 : 256);
-    for (int c = 0; c < nchunks; ++c) {
-        const int s = c & 1;
-        uint8_t* sA = sbase + s * C::STAGE;
-        uint8_t* sB = sA + C::A_BYTES;
-        if (c >= 2) {
-            mbar_wait(&mbar[s], parity[s]);
-            parity[s] ^= 1u;
-        }
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(p.ptrs[e]);
+    if (wid == 8) tmem_alloc(tslot, 512);
+    if (tid == 9 * 32) {
+        // full_a: one arrival (expect_tx) + TMA bytes; full_b: 256 decoder arrivals; empty / done: tcgen05.commit
+        for (int i = 0; i < 3 * NST + 1; ++i) mbar_init(&full_a[i], (i >= NST && i < 2 * NST) ? 256u : 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        prefetch_tmap(&tmA);
+    }
+    if (tid < 256) {
         if (PHASE == 0) {
-            for (int q = tid; q < 2 * 2 * 128 * 8; q += 256) {
-                int ch = q & 7, r = (q >> 3) & 127, mt = (q >> 10) & 1, pjq = q >> 11;
-                if (mt >= nmt) continue;
-                const __half* src = p.xh + ((size_t)(row0 + mt * 128 + r) * 2 + pjq) * p.H + (size_t)c * 64 + ch * 8;
-                uint32_t dst = smem_u32(sA + (pjq * 2 + mt) * 16384 + sw128_off(r, ch * 8));
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+            for (int j = tid; j < 3 * 128; j += 256) {
+                int which = j >> 7, col = nb * 128 + (j & 127);
+                const __half* src = reinterpret_cast<const __half*>(
+                    blob + (which == 0 ? gm.off_svh_g() : which == 1 ? gm.off_svh_u() : gm.off_suh_d()));
+                vec[j] = src[col];
             }
         } else {
-            for (int q = tid; q < 2 * 128 * 8; q += 256) {
-                int ch = q & 7, r = (q >> 3) & 127, mt = q >> 10;
-                if (mt >= nmt) continue;
-                const __half* src = p.abuf + (size_t)(row0 + mt * 128 + r) * p.I + (size_t)c * 64 + ch * 8;
-                uint32_t dst = smem_u32(sA + mt * 16384 + sw128_off(r, ch * 8));
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-            }
+            vec[tid] = reinterpret_cast<const __half*>(blob + gm.off_svh_d())[nb * 256 + tid];
         }
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-        bwork_decode_any(Kw, bw, c, nchunks, sB + (PHASE == 0 ? pj * 16384 : 0));
-        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (wid < 8) {
+        // ---- B decoders
+        const int Kw = PHASE == 0 ? (wid >> 2 ? ku : kg) : kd;
+        if (Kw < 2 || Kw > 5) { if (lane == 0) set_error(kErrGeometry); }
+        const uint32_t* words = reinterpret_cast<const uint32_t*>(blob);
+        DecCtx d;
+        if (PHASE == 0) {
+            const int pj = wid >> 2, ctl = (wid & 3) * 2;
+            d.wbase = words + (pj ? (size_t)(gm.I / 16) * 8 * gm.Kg : 0);
+            d.row_words = gm.gu_row_words();
+            d.ctg = nb * 8 + ctl;
+            d.sboff = (uint32_t)pj * 16384u + (uint32_t)ctl * 2048u;
+        } else {
+            const int ctl = wid * 2;
+            d.wbase = words + gm.gu_words();
+            d.row_words = gm.d_row_words();
+            d.ctg = nb * 16 + ctl;
+            d.sboff = (uint32_t)ctl * 2048u;
+        }
+        decode_loop_any<PHASE>(Kw, d, sbase, full_b, empty, nchunks);
+    } else if (tid == 8 * 32) {
+        // ---- MMA issuer
+        const uint32_t idesc = idesc_f16(128, PHASE == 0 ? 128 : 256);
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c % NST;
+            const uint32_t ph = (uint32_t)(c / NST) & 1u;
+            mbar_wait(&full_a[s], ph);
+            mbar_wait(&full_b[s], ph);
             tc_fence_after();
-            const uint32_t aA = smem_u32(sA), aB = smem_u32(sB);
+            const uint32_t aA = smem_u32(sbase + s * C::STAGE), aB = aA + C::A_BYTES;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
                 const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
@@ -293,143 +350,148 @@ __device__ __forceinline__ void gemm_mainloop(const PrefillArgs& p, uint8_t* sba
                     }
                 }
             }
-            umma_commit(&mbar[s]);
+            umma_commit(&empty[s]);
         }
-    }
-    const int sl = (nchunks - 1) & 1;
-    mbar_wait(&mbar[sl], parity[sl]);
-    tc_fence_after();
-}
-
-// Epilogue helpers: the thread owns TMEM lane (row) 32*(wid%4) + lane of M-tile mt = wid / 4.
-__device__ __forceinline__ void tmem_row128(uint32_t taddr, float v[128]) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tmem_ld32(taddr + q * 32, v + q * 32);
-}
-
-template <int PHASE>
-__global__ void __launch_bounds__(256, 1) prefill_gemm_kernel(PrefillArgs p) {
-    using C = GemmCfg<PHASE>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* tail = sbase + 2 * C::STAGE;
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(tail);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(tail + 16);
-    __half* vec = reinterpret_cast<__half*>(tail + 64);   // epilogue vectors (3 x 128 or 256 fp16)
-    const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
-    pdl_wait();
-    pdl_trigger();
-    const int NB = PHASE == 0 ? p.I / 128 : p.H / 256;
-    const int n_tiles = *p.n_tiles;
-    const int b = blockIdx.x;
-    if (b >= n_tiles * NB) return;
-    const int tv = p.tiles[b / NB], nb = b % NB;
-    const int a = tv & 0xFFFF, mp = tv >> 16;
-    const int e = p.act_expert[a], cnt = p.act_cnt[a];
-    const int row0 = p.act_start[a] + mp * 256;
-    const int rows = min(256, cnt - mp * 256);
-    int kg, ku, kd;
-    expert_kv(p, e, kg, ku, kd);
-    const Geom gm{p.H, p.I, kg, ku, kd};
-    const int Kw = PHASE == 0 ? (wid >> 2 ? ku : kg) : kd;   // this warp's tensor K (gate / up / down)
-    if (wid == 0) tmem_alloc(tslot, 512);
-    if (tid == 32) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    // epilogue vectors into shared memory
-    const uint8_t* blob = reinterpret_cast<const uint8_t*>(p.ptrs[e]);
-    if (PHASE == 0) {
-        for (int j = tid; j < 3 * 128; j += 256) {
-            int which = j >> 7, col = nb * 128 + (j & 127);
-            const __half* src = reinterpret_cast<const __half*>(blob + (which == 0 ? gm.off_svh_g() : which == 1 ? gm.off_svh_u()
-                                                                                                     : gm.off_suh_d()));
-            vec[j] = src[col];
-        }
-    } else {
-        for (int j = tid; j < 256; j += 256) vec[j] = reinterpret_cast<const __half*>(blob + gm.off_svh_d())[nb * 256 + j];
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tbase = *tslot;
-    // mixed-K experts: every warp decodes with its own tensor's K (gate/up halves can differ)
-    if (Kw < 2 || Kw > 5) { if (lane == 0) set_error(kErrGeometry); }
-    gemm_mainloop<PHASE>(p, sbase, mbar, tbase, e, row0, rows, nb, gm, Kw);
-    // ---- epilogue
-    const int mt = wid >> 2;
-    const int rloc = 32 * (wid & 3) + lane;
-    const bool valid = mt * 128 + rloc < rows;
-    const uint32_t tl = tbase + ((uint32_t)(32 * (wid & 3)) << 16);
-    float v[128];
-    if (PHASE == 0) {
-        const int pr = row0 + mt * 128 + rloc;
-        uint32_t gh[64];
-        tmem_row128(tl + (uint32_t)((mt * 2 + 0) * 128), v);
-        fwht128_regs(v);
-#pragma unroll
-        for (int j = 0; j < 128; j += 2) {
-            float g0 = rn16(v[j] * kRsqrt128 * __half2float(vec[j]));
-            float g1 = rn16(v[j + 1] * kRsqrt128 * __half2float(vec[j + 1]));
-            __half2 h = __floats2half2_rn(g0, g1);
-            gh[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        tmem_row128(tl + (uint32_t)((mt * 2 + 1) * 128), v);
-        fwht128_regs(v);
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-            float u = rn16(v[j] * kRsqrt128 * __half2float(vec[128 + j]));
-            __half2 h2 = *reinterpret_cast<__half2*>(&gh[j >> 1]);
-            float g = (j & 1) ? __high2float(h2) : __low2float(h2);
-            float sl = g / (1.0f + expf(-g)) * u;
-            sl = rn16(sl);
-            v[j] = rn16(sl * __half2float(vec[256 + j]));
-        }
-        fwht128_regs(v);
-        if (valid) {
-            uint4* op = reinterpret_cast<uint4*>(p.abuf + (size_t)pr * p.I + (size_t)nb * 128);
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                uint4 o;
-                uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    __half2 h = __floats2half2_rn(v[q * 8 + 2 * j] * kRsqrt128, v[q * 8 + 2 * j + 1] * kRsqrt128);
-                    ow[j] = *reinterpret_cast<uint32_t*>(&h);
-                }
-                op[q] = o;
-            }
-        }
-    } else {
-        const int pr = row0 + mt * 128 + rloc;
-        const float wt = valid ? p.pair_w[pr] : 0.0f;
+        umma_commit(done);
+    } else if (tid == 9 * 32) {
+        // ---- A producer (TMA)
+        const uint32_t bytes = (uint32_t)(PHASE == 0 ? 2 : 1) * (uint32_t)nmt * 16384u;
 #pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
-            tmem_row128(tl + (uint32_t)(mt * 256 + hb * 128), v);
-            fwht128_regs(v);
-            if (valid) {
-                uint4* op = reinterpret_cast<uint4*>(p.y + (size_t)pr * p.H + (size_t)nb * 256 + hb * 128);
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c % NST;
+            if (c >= NST) mbar_wait(&empty[s], (uint32_t)((c / NST) - 1) & 1u);
+            uint8_t* sA = sbase + s * C::STAGE;
+            mbar_arrive_expect_tx(&full_a[s], bytes);
+            if (PHASE == 0) {
+                for (int q = 0; q < 2; ++q)
+                    for (int mt = 0; mt < nmt; ++mt)
+                        tma_load_2d(sA + (q * 2 + mt) * 16384, &tmA, c * 64, q * p.Prow + row0 + mt * 128, &full_a[s]);
+            } else {
+                for (int mt = 0; mt < nmt; ++mt)
+                    tma_load_2d(sA + mt * 16384, &tmA, c * 64, row0 + mt * 128, &full_a[s]);
+            }
+        }
+        // every load issued has landed before the CTA can exit (bounded)
+        for (int c = max(0, nchunks - NST); c < nchunks; ++c) mbar_wait(&full_a[c % NST], (uint32_t)(c / NST) & 1u);
+    }
+
+    // ---- epilogue (warps 0-7)
+    if (wid < 8) {
+        mbar_wait(done, 0);
+        tc_fence_after();
+        const int mt = wid >> 2;
+        const int rloc = 32 * (wid & 3) + lane;
+        const bool valid = mt * 128 + rloc < rows;
+        const uint32_t tl = tbase + ((uint32_t)(32 * (wid & 3)) << 16);
+        const int pr = row0 + mt * 128 + rloc;
+        float v[128];
+        if (PHASE == 0) {
+            // the stages are free after `done`: per row, g (fp16) at stg, u (fp16) at stu, 16-byte chunks swizzled.
+            // Three passes share one FWHT: gate (TMEM) -> g, up (TMEM) -> u then SwiGLU, a (stg) -> abuf.
+            uint8_t* stg = sbase + tid * 256;
+            uint8_t* stu = sbase + 65536 + tid * 256;
+#pragma unroll 1
+            for (int pass = 0; pass < 3; ++pass) {
+                if (pass < 2) {
+                    tmem_row128(tl + (uint32_t)((mt * 2 + pass) * 128), v);
+                } else {
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    uint4 o;
-                    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+                    for (int q = 0; q < 16; ++q) {
+                        const uint4 aq = *reinterpret_cast<const uint4*>(stg + ((q ^ (tid & 15)) << 4));
+                        const uint32_t aw[4] = {aq.x, aq.y, aq.z, aq.w};
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        int c0 = hb * 128 + q * 8 + 2 * j;
-                        float y0 = v[q * 8 + 2 * j] * (kRsqrt128 * wt) * __half2float(vec[c0]);
-                        float y1 = v[q * 8 + 2 * j + 1] * (kRsqrt128 * wt) * __half2float(vec[c0 + 1]);
-                        __half2 h = __floats2half2_rn(y0, y1);
-                        ow[j] = *reinterpret_cast<uint32_t*>(&h);
+                        for (int jj = 0; jj < 8; ++jj)
+                            v[q * 8 + jj] = __half2float(__ushort_as_half((unsigned short)(aw[jj >> 1] >> (16 * (jj & 1)))));
                     }
-                    op[q] = o;
+                }
+                fwht128_regs(v);
+                if (pass < 2) {
+                    const __half* sv = vec + pass * 128;
+                    uint8_t* st = pass ? stu : stg;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        uint4 o;
+                        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const int j = q * 8 + 2 * jj;
+                            __half2 h = __floats2half2_rn(v[j] * kRsqrt128 * __half2float(sv[j]),
+                                                          v[j + 1] * kRsqrt128 * __half2float(sv[j + 1]));
+                            ow[jj] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        *reinterpret_cast<uint4*>(st + ((q ^ (tid & 15)) << 4)) = o;
+                    }
+                } else if (valid) {
+                    uint4* op = reinterpret_cast<uint4*>(p.abuf + (size_t)pr * p.I + (size_t)nb * 128);
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        uint4 o;
+                        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            __half2 h = __floats2half2_rn(v[q * 8 + 2 * jj] * kRsqrt128, v[q * 8 + 2 * jj + 1] * kRsqrt128);
+                            ow[jj] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        op[q] = o;
+                    }
+                }
+                if (pass == 1) {
+                    // SwiGLU and suh_d, 8 values at a time: a = fp16(fp16(silu(g) u) suh_d), written over g
+#pragma unroll 2
+                    for (int q = 0; q < 16; ++q) {
+                        const uint32_t off = (uint32_t)((q ^ (tid & 15)) << 4);
+                        const uint4 gq = *reinterpret_cast<const uint4*>(stg + off);
+                        const uint4 uq = *reinterpret_cast<const uint4*>(stu + off);
+                        const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+                        uint32_t ow[4];
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const __half2 g2 = *reinterpret_cast<const __half2*>(&gw[jj]);
+                            const __half2 u2 = *reinterpret_cast<const __half2*>(&uw[jj]);
+                            const int j = q * 8 + 2 * jj;
+                            float g0 = __low2float(g2), g1 = __high2float(g2);
+                            float a0 = rn16(g0 / (1.0f + expf(-g0)) * __low2float(u2));
+                            float a1 = rn16(g1 / (1.0f + expf(-g1)) * __high2float(u2));
+                            __half2 h = __floats2half2_rn(a0 * __half2float(vec[256 + j]), a1 * __half2float(vec[256 + j + 1]));
+                            ow[jj] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        *reinterpret_cast<uint4*>(stg + off) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+                    }
+                }
+            }
+        } else {
+            const float wt = valid ? p.pair_w[pr] : 0.0f;
+#pragma unroll 1
+            for (int hb = 0; hb < 2; ++hb) {
+                tmem_row128(tl + (uint32_t)(mt * 256 + hb * 128), v);
+                fwht128_regs(v);
+                if (valid) {
+                    uint4* op = reinterpret_cast<uint4*>(p.y + (size_t)pr * p.H + (size_t)nb * 256 + hb * 128);
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        uint4 o;
+                        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const int c0 = hb * 128 + q * 8 + 2 * jj;
+                            float y0 = v[q * 8 + 2 * jj] * (kRsqrt128 * wt) * __half2float(vec[c0]);
+                            float y1 = v[q * 8 + 2 * jj + 1] * (kRsqrt128 * wt) * __half2float(vec[c0 + 1]);
+                            __half2 h = __floats2half2_rn(y0, y1);
+                            ow[jj] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        op[q] = o;
+                    }
                 }
             }
         }
     }
+    __syncwarp();   // warps 8, 9: lanes 1-31 wait here for the lane that ran the MMA / TMA loop
     tc_fence_before();
     __syncthreads();
-    if (wid == 0) tmem_dealloc(tbase, 512);
+    if (wid == 8) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ combine
@@ -469,7 +531,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillArgs p) {
 // ------------------------------------------------------------------------------------------------ host
 struct PfLayout {
     size_t ib, fb, scr, tiles, ntiles, xh, abuf, y, total;
-    int A, mxb;
+    int A, mxb, Prow;
 };
 
 static size_t al1k(size_t v) { return (v + 1023) & ~(size_t)1023; }
@@ -484,29 +546,61 @@ static PfLayout pf_layout(int M, int topk, int H, int I, int E) {
     L.A = (int)std::min<size_t>(P, (size_t)E);
     const int pad = 256;
     L.mxb = (int)((P + pad - 1) / pad) + L.A;
+    L.Prow = (int)(P + 256);   // xh / abuf rows: the last tile reads up to 255 rows past the final pick
     size_t o = 0;
     L.ib = o; o += al1k((4 * (size_t)L.A + 1 + 2 * P + 16 + L.mxb + 1) * 4);
     L.fb = o; o += al1k(std::max<size_t>(P, 1) * 4);
     L.scr = o; o += al1k((size_t)exl3b_align_scratch((int)P, E));
     L.tiles = o; o += al1k(((P + 255) / 256 + L.A + 1) * 4);
     L.ntiles = o; o += 1024;
-    L.xh = o; o += al1k((P + 256) * 2 * (size_t)H * 2);
-    L.abuf = o; o += al1k((P + 256) * (size_t)I * 2);
+    L.xh = o; o += al1k((size_t)L.Prow * 2 * (size_t)H * 2);
+    L.abuf = o; o += al1k((size_t)L.Prow * (size_t)I * 2);
     L.y = o; o += al1k(P * (size_t)H * 2);
     L.total = o;
     return L;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D fp16 row-major [rows][inner] map with 64 x 128 boxes in the 128-byte swizzle (one K-major UMMA operand tile).
+static int make_tmap(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+    if (!enc) return exl3b_fail(EXL3B_ECUDA, "exl3b_moe_prefill: cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return exl3b_fail(EXL3B_ECUDA, "exl3b_moe_prefill: cuTensorMapEncodeTiled failed");
+    return 0;
+}
+
 template <int PHASE>
-static int launch_gemm(const PrefillArgs& p, int grid, cudaStream_t s) {
+static int launch_gemm(const PrefillArgs& p, const CUtensorMap& tm, int grid, cudaStream_t s) {
     using C = GemmCfg<PHASE>;
-    static bool attr = false;
-    if (!attr) {
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
         cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel<PHASE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
-        attr = true;
+        attr_dev = dev;
     }
-    cudaError_t e = launch_k(prefill_gemm_kernel<PHASE>, dim3(grid), dim3(256), (size_t)C::SMEM, s, p);
+    cudaError_t e = launch_k(prefill_gemm_kernel<PHASE>, dim3(grid), dim3(C::THREADS), (size_t)C::SMEM, s, p, tm);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     return 0;
 }
@@ -533,6 +627,7 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     EXL3B_CHECK(E >= 1 && E <= 1024, "exl3b_moe_prefill: 1 <= n_experts <= 1024");
     EXL3B_CHECK(kinfo || (K >= 2 && K <= 5), "exl3b_moe_prefill: K must be 2..5 (or pass kinfo)");
     EXL3B_CHECK(topk >= 1 && M >= 0, "exl3b_moe_prefill: bad M / topk");
+    EXL3B_CHECK((long long)M * topk + 256 < (1ll << 30), "exl3b_moe_prefill: too many picks");
     EXL3B_CHECK((((uintptr_t)x) & 15) == 0 && (x_stride % 8) == 0 && x_stride >= H, "exl3b_moe_prefill: x alignment / stride");
     EXL3B_CHECK((((uintptr_t)out) & 15) == 0 && (out_stride % 8) == 0 && out_stride >= H, "exl3b_moe_prefill: out alignment / stride");
     EXL3B_CHECK(out_bf16 >= 0 && out_bf16 <= 2, "exl3b_moe_prefill: out dtype code 0 fp16, 1 bf16, 2 fp32");
@@ -549,7 +644,7 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     if (rc) return rc;
     PrefillArgs p{};
     p.x = x; p.xs = x_stride; p.x_bf16 = x_bf16;
-    p.M = M; p.topk = topk; p.P = P;
+    p.M = M; p.topk = topk; p.P = P; p.Prow = L.Prow;
     p.ptrs = ptrs; p.kinfo = kinfo;
     p.H = H; p.I = I; p.K = K; p.E = E;
     p.out = out; p.os = out_stride; p.out_bf16 = out_bf16;
@@ -558,15 +653,19 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     p.pair_tok = ib + 4 * A + 1; p.pair_of = p.pair_tok + P; p.pair_w = (const float*)(b + L.fb);
     p.tiles = (int*)(b + L.tiles); p.n_tiles = (int*)(b + L.ntiles);
     p.xh = (__half*)(b + L.xh); p.abuf = (__half*)(b + L.abuf); p.y = (__half*)(b + L.y);
+    CUtensorMap tm_xh, tm_ab;
+    rc = make_tmap(&tm_xh, p.xh, (uint64_t)H, (uint64_t)2 * L.Prow);
+    if (rc) return rc;
+    rc = make_tmap(&tm_ab, p.abuf, (uint64_t)I, (uint64_t)L.Prow);
+    if (rc) return rc;
     cudaError_t e = launch_k(tiles_kernel, dim3(1), dim3(1024), 0, s, p);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
-    long long nh = (long long)P * 2 * (H / 128);
-    e = launch_k(had_in_kernel, dim3((unsigned)((nh + 127) / 128)), dim3(128), 0, s, p);
+    e = launch_k(had_in_kernel, dim3((unsigned)((P + 7) / 8)), dim3(256), 0, s, p);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     const int max_tiles = (P + 255) / 256 + A;
-    rc = launch_gemm<0>(p, max_tiles * (I / 128), s);
+    rc = launch_gemm<0>(p, tm_xh, max_tiles * (I / 128), s);
     if (rc) return rc;
-    rc = launch_gemm<1>(p, max_tiles * (H / 256), s);
+    rc = launch_gemm<1>(p, tm_ab, max_tiles * (H / 256), s);
     if (rc) return rc;
     long long nc = (long long)M * (H / 8);
     e = launch_k(prefill_combine_kernel, dim3((unsigned)((nc + 255) / 256)), dim3(256), 0, s, p);

@@ -19,7 +19,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Wait until the mbarrier phase with the given parity has completed.  Bounded: after ~1 s the wait gives up, sets
-// kErrWait in the device status word and returns false (the caller continues; its results are then invalid).
+// kErrWait in the device status word and returns false (the caller continues; its results are then invalid).  Once
+// kErrWait is set anywhere on the device, every other wait gives up at its next time check, so a failed launch ends
+// within about a second instead of timing out wait by wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
     uint64_t t0 = 0;
@@ -32,6 +34,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "memory");
         if (ok) return true;
         if ((it & 255) == 0) {
+            if (*reinterpret_cast<volatile int*>(&g_status) & kErrWait) return false;
             uint64_t t = globaltimer_ns();
             if (t0 == 0) t0 = t;
             else if (t - t0 > 1000000000ull) {
@@ -110,6 +113,36 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // Byte offset of fp16 element (row, k) (k in 0..63) inside a K-major SWIZZLE_128B tile.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
     return (uint32_t)row * 128u + ((((uint32_t)k >> 3) ^ ((uint32_t)row & 7u)) << 4) + (((uint32_t)k & 7u) << 1);
+}
+
+// ------------------------------------------------------------------------------------------------ arrivals, TMA
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 2-D tiled TMA load of one box into this CTA's shared memory, completing `bytes` on `bar` (no multicast: the source
+// is this GPU's own memory and the destination this CTA only).  x (innermost coordinate) must be a multiple of
+// 16 bytes / element size.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// Four 8x8 fp16 matrices from the mma fragment layout (register q of lane l: row l/4, columns 2(l%4), +1) to shared
+// memory; lane l gives the address of row l%8 of matrix l/8.
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
 }
 
 }  // namespace exl3b
