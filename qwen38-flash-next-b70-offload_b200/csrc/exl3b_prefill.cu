@@ -74,55 +74,84 @@ __global__ void __launch_bounds__(1024) tiles_kernel(PrefillArgs p) {
 }
 
 // ------------------------------------------------------------------------------------------------ had_in
-// One warp per sorted pick: the token row is read once for both projections; each 128-block is held as 4 values per
-// lane and transformed with the in-warp FWHT (same butterfly order as the reference).
+// One warp per sorted pick, 32 blocks of 8 warps per 256-row tile (the tile gives the expert); 8 128-blocks per warp
+// step: lane l holds 32 consecutive values (quarter l%4) of block l/4.  FWHT strides 1..16 run inside the lane,
+// strides 32 and 64 pair lanes l^1 and l^2 (the reference's butterfly order, stage by stage).
 __global__ void __launch_bounds__(256) had_in_kernel(PrefillArgs p) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
-    const long long prl = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (prl >= p.P) return;
-    const int pr = (int)prl;
-    const int na = *p.n_act;
-    int lo = 0, hi = na - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (p.act_start[mid] <= pr) lo = mid; else hi = mid - 1;
-    }
-    const int e = p.act_expert[lo];
+    const int tile = blockIdx.x >> 5;
+    if (tile >= *p.n_tiles) return;
+    const int tv = p.tiles[tile];
+    const int a = tv & 0xFFFF, r = (tv >> 16) * 256 + (blockIdx.x & 31) * 8 + (threadIdx.x >> 5);
+    if (r >= p.act_cnt[a]) return;
+    const int pr = p.act_start[a] + r;
+    const int e = p.act_expert[a];
     int kg, ku, kd;
     expert_kv(p, e, kg, ku, kd);
     const Geom gm{p.H, p.I, kg, ku, kd};
     const uint8_t* blob = reinterpret_cast<const uint8_t*>(p.ptrs[e]);
     const int tok = p.pair_tok[pr];
     const uint16_t* xr = reinterpret_cast<const uint16_t*>(p.x) + (size_t)tok * p.xs;
+    const int nblk = p.H / 128, g = lane >> 2, sub = lane & 3;
 #pragma unroll 1
     for (int proj = 0; proj < 2; ++proj) {
-        const __half* suh = reinterpret_cast<const __half*>(blob + gm.off_suh_g() + (size_t)proj * p.H * 2);
+        const uint16_t* suh = reinterpret_cast<const uint16_t*>(blob + gm.off_suh_g() + (size_t)proj * p.H * 2);
         __half* dst = p.xh + ((size_t)proj * p.Prow + pr) * p.H;
-#pragma unroll 2
-        for (int kb = 0; kb < p.H / 128; ++kb) {
-            const int i0 = kb * 128 + lane * 4;
-            uint2 xv = *reinterpret_cast<const uint2*>(xr + i0);
-            uint2 sv = __ldg(reinterpret_cast<const uint2*>(suh + i0));
-            float xf[4];
-            if (p.x_bf16) {
-                xf[0] = __uint_as_float(xv.x << 16); xf[1] = __uint_as_float(xv.x & 0xFFFF0000u);
-                xf[2] = __uint_as_float(xv.y << 16); xf[3] = __uint_as_float(xv.y & 0xFFFF0000u);
-            } else {
-                __half2 h0 = *reinterpret_cast<__half2*>(&xv.x), h1 = *reinterpret_cast<__half2*>(&xv.y);
-                xf[0] = __low2float(h0); xf[1] = __high2float(h0); xf[2] = __low2float(h1); xf[3] = __high2float(h1);
+#pragma unroll 1
+        for (int kb0 = 0; kb0 < nblk; kb0 += 8) {
+            const int kb = kb0 + g;
+            const bool act = kb < nblk;
+            const int i0 = kb * 128 + sub * 32;
+            float v[32];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 xv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
+                if (act) {
+                    xv = *reinterpret_cast<const uint4*>(xr + i0 + q * 8);
+                    sv = __ldg(reinterpret_cast<const uint4*>(suh + i0 + q * 8));
+                }
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    const uint32_t xb = (xw[h >> 1] >> (16 * (h & 1))) & 0xFFFFu;
+                    const float xf = p.x_bf16 ? __uint_as_float(xb << 16) : __half2float(__ushort_as_half((unsigned short)xb));
+                    const float sf = __half2float(__ushort_as_half((unsigned short)((sw[h >> 1] >> (16 * (h & 1))) & 0xFFFFu)));
+                    v[q * 8 + h] = rn16(xf * sf);
+                }
             }
-            __half2 s0 = *reinterpret_cast<__half2*>(&sv.x), s1 = *reinterpret_cast<__half2*>(&sv.y);
-            float v[4] = {rn16(xf[0] * __low2float(s0)), rn16(xf[1] * __high2float(s0)), rn16(xf[2] * __low2float(s1)),
-                          rn16(xf[3] * __high2float(s1))};
-            fwht128_warp(v, lane);
-            __half2 o0 = __floats2half2_rn(v[0] * kRsqrt128, v[1] * kRsqrt128);
-            __half2 o1 = __floats2half2_rn(v[2] * kRsqrt128, v[3] * kRsqrt128);
-            uint2 o;
-            o.x = *reinterpret_cast<uint32_t*>(&o0);
-            o.y = *reinterpret_cast<uint32_t*>(&o1);
-            *reinterpret_cast<uint2*>(dst + i0) = o;
+#pragma unroll
+            for (int hs = 1; hs < 32; hs <<= 1)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2 * hs)
+#pragma unroll
+                    for (int j = i; j < i + hs; ++j) {
+                        const float a = v[j], b = v[j + hs];
+                        v[j] = a + b;
+                        v[j + hs] = a - b;
+                    }
+#pragma unroll
+            for (int m = 1; m <= 2; m <<= 1) {
+                const bool upper = (lane & m) != 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
+                    v[j] = upper ? (o - v[j]) : (v[j] + o);
+                }
+            }
+            if (act) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t ow[4];
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        __half2 h = __floats2half2_rn(v[q * 8 + 2 * jj] * kRsqrt128, v[q * 8 + 2 * jj + 1] * kRsqrt128);
+                        ow[jj] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    *reinterpret_cast<uint4*>(dst + i0 + q * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+                }
+            }
         }
     }
 }
@@ -375,8 +404,8 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
         for (int c = max(0, nchunks - NST); c < nchunks; ++c) mbar_wait(&full_a[c % NST], (uint32_t)(c / NST) & 1u);
     }
 
-    // ---- epilogue (warps 0-7)
-    if (wid < 8) {
+    // ---- epilogue (warps 0-7); a warp whose 32 rows are all past the tile's row count has nothing to store
+    if (wid < 8 && (wid >> 2) * 128 + 32 * (wid & 3) < rows) {
         mbar_wait(done, 0);
         tc_fence_after();
         const int mt = wid >> 2;
@@ -450,8 +479,10 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
                             const __half2 u2 = *reinterpret_cast<const __half2*>(&uw[jj]);
                             const int j = q * 8 + 2 * jj;
                             float g0 = __low2float(g2), g1 = __high2float(g2);
-                            float a0 = rn16(g0 / (1.0f + expf(-g0)) * __low2float(u2));
-                            float a1 = rn16(g1 / (1.0f + expf(-g1)) * __high2float(u2));
+                            // SiLU with the hardware exp2 / reciprocal approximations (~2 ulp of fp32, far below the
+                            // fp16 rounding that follows)
+                            float a0 = rn16(__fdividef(g0, 1.0f + __expf(-g0)) * __low2float(u2));
+                            float a1 = rn16(__fdividef(g1, 1.0f + __expf(-g1)) * __high2float(u2));
                             __half2 h = __floats2half2_rn(a0 * __half2float(vec[256 + j]), a1 * __half2float(vec[256 + j + 1]));
                             ow[jj] = *reinterpret_cast<uint32_t*>(&h);
                         }
@@ -660,9 +691,9 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     if (rc) return rc;
     cudaError_t e = launch_k(tiles_kernel, dim3(1), dim3(1024), 0, s, p);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
-    e = launch_k(had_in_kernel, dim3((unsigned)((P + 7) / 8)), dim3(256), 0, s, p);
-    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     const int max_tiles = (P + 255) / 256 + A;
+    e = launch_k(had_in_kernel, dim3((unsigned)max_tiles * 32u), dim3(256), 0, s, p);
+    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     rc = launch_gemm<0>(p, tm_xh, max_tiles * (I / 128), s);
     if (rc) return rc;
     rc = launch_gemm<1>(p, tm_ab, max_tiles * (H / 256), s);
