@@ -30,6 +30,8 @@ H, I, E, TOPK, K, L, S = 2048, 768, 512, 10, 3, 48, 8000
 SEED = 0
 GU_BYTES = (H // 16) * (2 * I // 16) * 8 * K * 4     # gate|up codes per expert: 1,179,648 B
 BLOB = 1786368
+PF_T = 8192          # configs[2] prefill chunk
+PF_KEY0 = 1 << 20    # blob keys of the prefill layer (distinct from the decode stack's)
 # router weight std: x . Wr then has the std of a standard Gumbel variable (pi / sqrt(6) = 1.28), so -1.1 ln(rank) +
 # router noise makes each layer's top-10 a Zipf(1.1)-like Plackett-Luce sample and picks miss the 8,000-slot cache
 WR_STD = 1.2825498 / (2048 ** 0.5)
@@ -152,23 +154,13 @@ def step_fn(st, wr, bias, xs, outs, routes):
         routes.append((ids, w))
 
 
-def run_ours(args):
+def measure_decode(st, wr, bias, xs, ring, args, dev, local, clocks=True):
+    """Graph-captured decode step timed over args.steps replays (device time), then end to end through the public
+    ops with pinned-host inputs and outputs, then the per-phase device time of an eager pass (profile events)."""
+    import ctypes
     import torch
-    import torch.distributed as dist
     from exl3b200 import _lib
-    from exl3b200 import ops as X
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    X.register()
-    T = args.batch
-    st, wr, bias, xs, ring = build_stack(dev, T)
+    T = xs.shape[1]
     outs = torch.empty_like(xs)
     routes = []
     # warm-up (also the cache's LRU history), then capture
@@ -188,21 +180,19 @@ def run_ours(args):
     for _ in range(args.warmup):
         g.replay()
     ring0 = int(ring[0].item())
-    if world > 1:
-        dist.barrier()
     torch.cuda.synchronize(dev)
-    clk = Clocks(local)
-    clk.start()
+    clk = Clocks(local) if clocks else None
+    if clk:
+        clk.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         g.replay()
     e1.record()
     torch.cuda.synchronize(dev)
-    clocks = clk.stop()
+    clk_rec = clk.stop() if clk else None
     ms = e0.elapsed_time(e1) / args.steps
     masked = (int(ring[0].item()) - ring0) / (args.steps * L * T * TOPK)
-    # distinct non-masked experts per layer (algorithmic bytes), from the last step's routing
     id_buf = torch.stack([r[0] for r in graph_routes])
     w_buf = torch.stack([r[1] for r in graph_routes])
     ids_np, w_np = id_buf.cpu().numpy(), w_buf.cpu().numpy()
@@ -220,9 +210,8 @@ def run_ours(args):
     e3.record()
     torch.cuda.synchronize(dev)
     ms_e2e = e2.elapsed_time(e3) / args.steps
-    # roofline of the dominant kernel (gate-up): phase CUDA events recorded by the library around its kernels on the
-    # launch stream, in an eager pass of the same step queued behind a GPU sleep so no launch gap is timed
-    import ctypes
+    # per-phase device time: events recorded by the library around its kernels on the launch stream, in an eager pass
+    # of the same step queued behind a GPU sleep so that no launch gap is timed
     L_ = _lib.lib()
     keys = list(st.layer_index)
     gu_ms, dn_ms, rp_ms = [], [], []
@@ -243,12 +232,138 @@ def run_ours(args):
             rp_ms.append(evs[li][0].elapsed_time(evs[li][1]))
             gu_ms.append(evs[li][1].elapsed_time(evs[li][2]))
             dn_ms.append(evs[li][2].elapsed_time(evs[li][3]))
+    del g
+    return {"T": T, "ms": ms, "ms_e2e": ms_e2e, "masked": masked, "distinct": distinct, "id_buf": id_buf,
+            "w_buf": w_buf, "gu_ms": gu_ms, "dn_ms": dn_ms, "rp_ms": rp_ms, "clocks": clk_rec,
+            "h2d": int(xs.numel() * 2), "d2h": int(outs.numel() * 2)}
+
+
+def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T):
+    """one MoE layer, 8192-token prefill chunk, all 512 experts resident, router logits ~ N(0,1) plus a
+    per-expert N(0,1.5) bias.  The layer (moe_forward on the router's picks: the grouped tcgen05 GEMM path) is timed
+    with device events; e2e adds the host -> device copy of x and the device -> host copy of the output per call."""
+    import ctypes
+    import torch
+    from exl3b200 import _lib, synth
+    arena = torch.empty((E, BLOB), dtype=torch.uint8, device=dev)
+    synth.fill_blobs(arena, SEED, [PF_KEY0 + e for e in range(E)], H, I, K)
+    ptrs = (arena.data_ptr() + torch.arange(E, dtype=torch.int64) * BLOB).to(dev)
+    x = synth.activations(T, H, 3000).to(dev)
+    wr = synth.router_weight(E, H, 1.0 / H ** 0.5, SEED + 999).to(dev)
+    bias = synth.normal_bias(E, 1.5, SEED).to(dev)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record()
+    ids, w = torch.ops.exl3b200_moe.router_topk(x, wr, bias, TOPK)
+    r1.record()
+    torch.cuda.synchronize(dev)
+    router_ms = r0.elapsed_time(r1)
+    fwd = torch.ops.exl3b200_moe.moe_forward
+    for _ in range(warmup):
+        out = fwd(x, ids, w, ptrs, I, K, E)
+    torch.cuda.synchronize(dev)
+    clk = Clocks(local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        out = fwd(x, ids, w, ptrs, I, K, E)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clk_rec = clk.stop()
+    ms = e0.elapsed_time(e1) / iters
+    hx = x.cpu().pin_memory()
+    ho = torch.empty_like(out, device="cpu").pin_memory()
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(iters):
+        x.copy_(hx, non_blocking=True)
+        out = fwd(x, ids, w, ptrs, I, K, E)
+        ho.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms_e2e = e0.elapsed_time(e1) / iters
+    # phase times of the library's launches (align .. input transform | gate-up GEMM | down GEMM + combine)
+    L_ = _lib.lib()
+    ph = [[], [], []]
+    for _ in range(3):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        for ev in evs:
+            ev.record()
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(int(20e6))
+        L_.exl3b_set_profile_events(*[ctypes.c_void_p(ev.cuda_event) for ev in evs])
+        fwd(x, ids, w, ptrs, I, K, E)
+        L_.exl3b_set_profile_events(None, None, None, None)
+        torch.cuda.synchronize(dev)
+        for k in range(3):
+            ph[k].append(evs[k].elapsed_time(evs[k + 1]))
+    ph = [sum(v) / len(v) for v in ph]
+    cnt = torch.bincount(ids.flatten().long(), minlength=E)
+    _, tc, src = peaks()
+    flops = 2.0 * T * TOPK * 3 * H * I
+    gu_flops = 2.0 * T * TOPK * 2 * H * I
+    gu_ach = gu_flops / (ph[1] * 1e-3) / 1e12
+    del arena
+    return {"tokens": T, "value": round(T * 1000.0 / ms, 1), "unit": "tok/s (one layer)", "ms_per_layer": round(ms, 4),
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "layer_frac_of_peak": round(flops / (ms * 1e-3) / 1e12 / tc, 4),
+            "e2e": {"value": round(T * 1000.0 / ms_e2e, 1), "unit": "tok/s (one layer)",
+                    "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2)},
+            "roofline": {"bound": "tensor", "achieved": round(gu_ach, 1), "peak": tc, "unit": "TFLOP/s",
+                         "frac": round(gu_ach / tc, 4), "traffic": None, "kernel": "prefill_gemm_kernel<0>",
+                         "peak_source": src + " bf16 burst", "algorithmic_flops_per_launch": gu_flops,
+                         "avg_launch_us": round(ph[1] * 1e3, 1)},
+            "phase_us": {"align_transform": round(ph[0] * 1e3, 1), "gateup_gemm": round(ph[1] * 1e3, 1),
+                         "down_gemm_combine": round(ph[2] * 1e3, 1)},
+            "router_ms": round(router_ms, 3), "active_experts": int((cnt > 0).sum()), "max_picks": int(cnt.max()),
+            "launches_per_layer": 8, "clocks": clk_rec,
+            "config": "configs[2]: 1 layer, 8192 tokens, 512 experts resident, top-10, K=3, logits N(0,1) + bias N(0,1.5)"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from exl3b200 import synth
+    from exl3b200 import ops as X
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    X.register()
+    T = args.batch
+    st, wr, bias, xs, ring = build_stack(dev, T)
+    if world > 1:
+        dist.barrier()
+    d = measure_decode(st, wr, bias, xs, ring, args, dev, local)
+    ms, ms_e2e = d["ms"], d["ms_e2e"]
+    bs4 = None
+    if T == 1 and not args.no_bs4:
+        xs4 = torch.stack([synth.activations(4, H, 1000 + li) for li in range(L)]).to(dev)
+        d4 = measure_decode(st, wr, bias, xs4, ring, args, dev, local, clocks=False)
+        bs4 = {"value": round(world * 4 * 1000.0 / d4["ms"], 2), "unit": "tok/s", "ms_per_step": round(d4["ms"], 4),
+               "e2e": {"value": round(world * 4 * 1000.0 / d4["ms_e2e"], 2), "unit": "tok/s",
+                       "h2d_bytes_per_step": d4["h2d"], "d2h_bytes_per_step": d4["d2h"]},
+               "distinct_experts_per_layer": round(sum(d4["distinct"]) / L, 2),
+               "phase_us": {"route_prep": round(1e3 * sum(d4["rp_ms"]) / len(d4["rp_ms"]), 2),
+                            "gateup": round(1e3 * sum(d4["gu_ms"]) / len(d4["gu_ms"]), 2),
+                            "down_combine": round(1e3 * sum(d4["dn_ms"]) / len(d4["dn_ms"]), 2)}}
+        del xs4
+    X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32))
+    pf = None
+    if not args.no_prefill:
+        del st
+        torch.cuda.empty_cache()
+        pf = measure_prefill(dev, local)
     hbm, tc, src = peaks()
+    distinct = d["distinct"]
     avg_distinct = sum(distinct) / L
     gu_bytes = avg_distinct * GU_BYTES
-    gu_s = (sum(gu_ms) / len(gu_ms)) * 1e-3
+    gu_s = (sum(d["gu_ms"]) / len(d["gu_ms"])) * 1e-3
     ach = gu_bytes / gu_s / 1e9
-    tok_s = T * 1000.0 / ms
     # max over ranks; value = all ranks' tokens / slowest rank
     if world > 1:
         t = torch.tensor([ms, ms_e2e], device=dev)
@@ -264,26 +379,26 @@ def run_ours(args):
                    "H": H, "I": I, "experts": E, "topk": TOPK, "K": K, "slots": S, "keys": L * E,
                    "parallelism": f"replicas x{world}", "l2": "working set per step "
                    f"{step_bytes / 1e6:.0f} MB of codes > 126 MB L2 (no flush needed)",
-                   "masked_pick_fraction": round(masked, 4), "distinct_experts_per_layer": round(avg_distinct, 2)},
+                   "masked_pick_fraction": round(d["masked"], 4), "distinct_experts_per_layer": round(avg_distinct, 2)},
         "e2e": {"value": round(world * T * 1000.0 / ms_e2e, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": int(xs.numel() * 2), "d2h_bytes_per_step": int(outs.numel() * 2)},
+                "h2d_bytes_per_step": d["h2d"], "d2h_bytes_per_step": d["d2h"]},
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                     "traffic": None, "kernel": "gateup_kernel<3>", "peak_source": src,
+                     "traffic": None, "kernel": "stream_kernel<3,0> (decode gate-up)", "peak_source": src,
                      "algorithmic_bytes_per_launch": int(gu_bytes), "avg_launch_us": round(gu_s * 1e6, 2)},
         "layer_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
                       "frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
-                      "phase_us": {"route_prep": round(1e3 * sum(rp_ms) / len(rp_ms), 2),
-                                   "gateup": round(1e3 * sum(gu_ms) / len(gu_ms), 2),
-                                   "down_combine": round(1e3 * sum(dn_ms) / len(dn_ms), 2)}},
+                      "phase_us": {"route_prep": round(1e3 * sum(d["rp_ms"]) / len(d["rp_ms"]), 2),
+                                   "gateup": round(1e3 * sum(d["gu_ms"]) / len(d["gu_ms"]), 2),
+                                   "down_combine": round(1e3 * sum(d["dn_ms"]) / len(d["dn_ms"]), 2)}},
         "gpu_launches": args.steps * L * 4,
-        "clocks": clocks,
+        "clocks": d["clocks"],
     }
-    if args.batch == 1 and not args.no_bs4:
-        line["bs4"] = None   # filled below when requested
+    if bs4 is not None:
+        line["bs4"] = bs4
+    if pf is not None:
+        line["prefill"] = pf
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(st, xs, id_buf, w_buf, T, seconds=args.cpu_seconds)
-    X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32))
-    del g
+        line["cpu_baseline"] = cpu_baseline(d["id_buf"], d["w_buf"], T, seconds=args.cpu_seconds)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -300,32 +415,32 @@ def _oracle_layer_job(args):
     return O.moe_layer(x, ids, w, blobs, H, I, K)
 
 
-def cpu_baseline(st, xs, id_buf, w_buf, T, seconds=20.0):
-    """The CPU restatement (oracle/, C) on the host cores: layers of the bench step run in parallel threads (the C
-    code releases the GIL), until about `seconds` of wall time; tok/s extrapolated to the 48-layer step."""
+def cpu_baseline(id_buf, w_buf, T, seconds=20.0):
+    """The CPU restatement (oracle/, C) on the host cores: layers of the bench step (the GPU run's routing after the
+    cache mask; inputs and blobs regenerated from the same seeds) run in parallel threads (the C code releases the
+    GIL), until about `seconds` of wall time; tok/s extrapolated to the 48-layer step."""
     import concurrent.futures as cf
     import numpy as np
     import torch
+    from exl3b200 import synth
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     O.lib()
     threads = os.cpu_count() or 1
     ids_np, w_np = id_buf.cpu().numpy(), w_buf.cpu().numpy()
-    so = st.slot_of_dev.cpu().numpy()
+    nlay = max(1, min(L, 2 * threads))
     jobs = []
-    for li in range(L):
+    for li in range(nlay):
         blobs = [None] * E
         for e in set(int(v) for v in ids_np[li].ravel()):
-            s = int(so[li * E + e])
-            if s >= 0:
-                blobs[e] = st.slots[s].cpu().numpy()
-        xb = xs[li].cpu().view(torch.int16).numpy().view(np.uint16)
+            blobs[e] = synth.make_blob(SEED, li * E + e, H, I, K).numpy()
+        xb = synth.activations(T, H, 1000 + li).view(torch.int16).numpy().view(np.uint16)
         jobs.append((xb, ids_np[li].copy(), w_np[li].copy(), blobs))
     done = 0
     t0 = time.perf_counter()
     with cf.ThreadPoolExecutor(threads) as ex:
         while time.perf_counter() - t0 < seconds and done < 4 * L:
-            batch = [jobs[(done + i) % L] for i in range(threads)]
+            batch = [jobs[(done + i) % nlay] for i in range(threads)]
             list(ex.map(_oracle_layer_job, batch))
             done += len(batch)
     dt = time.perf_counter() - t0
@@ -391,6 +506,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-bs4", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:

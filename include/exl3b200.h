@@ -100,7 +100,8 @@ int exl3b_moe_decode_cached(const void* x, int64_t x_stride, int x_bf16, int32_t
                             int64_t ws_bytes, int flags, void* stream);
 /* Profiling hook (no reference counterpart; the reference times graph replays from the host,
  * plugin/sglang_plugin.tier.py:1036-1087): cudaEvent_t handles recorded by exl3b_moe_decode before its route
- * prep, gate-up and down kernels and after down.  NULL disables a slot.  Process-global, off by default. */
+ * prep, gate-up and down kernels and after down, and by exl3b_moe_prefill before align, before the gate-up GEMM,
+ * before the down GEMM and after the combine.  NULL disables a slot.  Process-global, off by default. */
 int exl3b_set_profile_events(void* before_route, void* before_gateup, void* before_down, void* after_down);
 
 /* ---- routing tables ------------------------------------------------------------------------------------------ */

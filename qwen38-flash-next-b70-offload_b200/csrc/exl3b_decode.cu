@@ -631,7 +631,7 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Optional phase events (profiling hook, off by default): recorded before prep, before gate-up, before down and
 // after down on the launch stream.  Process-global; set and cleared by exl3b_set_profile_events.
 static cudaEvent_t g_prof_ev[4] = {nullptr, nullptr, nullptr, nullptr};
-static inline void prof_record(int i, cudaStream_t s) {
+void prof_record(int i, cudaStream_t s) {
     if (g_prof_ev[i]) cudaEventRecord(g_prof_ev[i], s);
 }
 

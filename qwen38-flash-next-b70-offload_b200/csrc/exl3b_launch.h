@@ -24,6 +24,11 @@ inline bool pdl_enabled() {
     return v == 1;
 }
 
+// Profiling hook (exl3b_set_profile_events): records phase event i on stream s when one is set.  Decode: 0 before
+// the routing / cache step, 1 before gate-up, 2 before down, 3 after down.  Prefill: 0 before align, 1 before the
+// gate-up GEMM, 2 before the down GEMM, 3 after the combine.
+void prof_record(int i, cudaStream_t s);
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
     cudaLaunchConfig_t cfg = {};

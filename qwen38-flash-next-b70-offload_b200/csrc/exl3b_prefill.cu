@@ -670,6 +670,7 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     char* b = (char*)workspace;
     const int P = M * topk;
     int32_t* ib = (int32_t*)(b + L.ib);
+    prof_record(0, s);
     int rc = exl3b_align(ids, w, P, topk, E, 256, ib, (float*)(b + L.fb), L.A, L.mxb, b + L.scr,
                          exl3b_align_scratch(P, E), stream);
     if (rc) return rc;
@@ -694,12 +695,15 @@ extern "C" EXL3B_API int exl3b_moe_prefill(const void* x, int64_t x_stride, int 
     const int max_tiles = (P + 255) / 256 + A;
     e = launch_k(had_in_kernel, dim3((unsigned)max_tiles * 32u), dim3(256), 0, s, p);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    prof_record(1, s);
     rc = launch_gemm<0>(p, tm_xh, max_tiles * (I / 128), s);
     if (rc) return rc;
+    prof_record(2, s);
     rc = launch_gemm<1>(p, tm_ab, max_tiles * (H / 256), s);
     if (rc) return rc;
     long long nc = (long long)M * (H / 8);
     e = launch_k(prefill_combine_kernel, dim3((unsigned)((nc + 255) / 256)), dim3(256), 0, s, p);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    prof_record(3, s);
     return exl3b_launch_status("exl3b_moe_prefill");
 }
