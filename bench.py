@@ -383,7 +383,7 @@ def run_ours(args):
         "e2e": {"value": round(world * T * 1000.0 / ms_e2e, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": d["h2d"], "d2h_bytes_per_step": d["d2h"]},
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                     "traffic": None, "kernel": "stream_kernel<3,0> (decode gate-up)", "peak_source": src,
+                     "traffic": None, "kernel": "gu_cluster_kernel<3> (decode gate-up)", "peak_source": src,
                      "algorithmic_bytes_per_launch": int(gu_bytes), "avg_launch_us": round(gu_s * 1e6, 2)},
         "layer_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
                       "frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4),

@@ -97,8 +97,9 @@ __device__ __forceinline__ uint32_t mul1_pair(uint32_t st0, uint32_t st1) {
     uint32_t x0 = st0 * 0x83DCD12Du, x1 = st1 * 0x83DCD12Du;
     uint32_t h0 = __dp4a(x0, 0x01010101u, 0x6400u);   // unsigned byte dot product: 0x6400 + sum of the 4 bytes
     uint32_t h1 = __dp4a(x1, 0x01010101u, 0x6400u);
-    uint32_t hp;   // h1 * 65536 + h0 on the integer multiply-add pipe (h0 < 2^16)
-    asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(hp) : "r"(h1), "r"(h0));
+    // {lo = h0, hi = h1}: both are < 2^16, so a byte permute packs them (ALU pipe, off the multiply-add pipe that
+    // the multiplies and dp4a use)
+    uint32_t hp = __byte_perm(h0, h1, 0x5410);
     __half2 h = *reinterpret_cast<__half2*>(&hp);
     const __half2 c1 = __halves2half2(__ushort_as_half((unsigned short)0x1eee), __ushort_as_half((unsigned short)0x1eee));
     const __half2 c2 = __halves2half2(__ushort_as_half((unsigned short)0xc931), __ushort_as_half((unsigned short)0xc931));

@@ -51,10 +51,15 @@ struct DecodeArgs {
 
 // ------------------------------------------------------------------------------------------------ prep
 // Zero the arrival counters, group active picks by expert (ascending id, picks in ascending index), count active
-// picks per token and zero the output rows of tokens with none.  All 1024 threads of one block.
-__device__ void route_prep_block(const DecodeArgs& a) {
+// picks per token and zero the output rows of tokens with none.  All 1024 threads of one block; the picks pass
+// through shared memory in chunks of kPrepChunk (one expert per thread scans each chunk for its picks).
+constexpr int kPrepChunk = 2048;
+
+__device__ __forceinline__ void route_prep_block(const DecodeArgs& a) {
     __shared__ int cnt[1024];
     __shared__ int sh_warp2[32];
+    __shared__ int s_ids[kPrepChunk];
+    __shared__ float s_w[kPrepChunk];
     const int tid = threadIdx.x, npairs = a.M * a.topk;
     const int nbI = a.I / 128, nbH = a.H / 128;
     for (int i = tid; i < a.maxent * nbI; i += blockDim.x) a.cnt_gu[i] = 0;
@@ -63,24 +68,35 @@ __device__ void route_prep_block(const DecodeArgs& a) {
     if (tid == 0) a.blocks_done[0] = 0;
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int i = tid; i < npairs; i += blockDim.x) {
-        int e = a.ids[i];
-        bool ok = e >= 0 && e < a.E;
-        bool act = ok && !(a.skip_zero && a.w[i] == 0.0f);
-        if (!ok) set_error(kErrBounds);
-        a.pick_act[i] = act ? 1 : 0;
-        if (act) atomicAdd(&cnt[e], 1);
-    }
-    for (int m = tid; m < a.M; m += blockDim.x) {
-        int c = 0;
-        for (int k = 0; k < a.topk; ++k) {
-            int i = m * a.topk + k;
+    // pass 1: activity flags, per-expert counts, per-token counts (tokens never straddle a chunk)
+    const int chunk = (kPrepChunk / a.topk) * a.topk;
+    for (int c0 = 0; c0 < npairs; c0 += chunk) {
+        const int c1 = min(npairs, c0 + chunk);
+        for (int i = c0 + tid; i < c1; i += blockDim.x) {
             int e = a.ids[i];
-            c += ((e >= 0 && e < a.E) && !(a.skip_zero && a.w[i] == 0.0f)) ? 1 : 0;
+            bool ok = e >= 0 && e < a.E;
+            bool act = ok && !(a.skip_zero && a.w[i] == 0.0f);
+            if (!ok) set_error(kErrBounds);
+            a.pick_act[i] = act ? 1 : 0;
+            s_ids[i - c0] = act ? e : -1;
+            if (act) atomicAdd(&cnt[e], 1);
         }
-        a.tok_cnt[m] = c;
+        __syncthreads();
+        for (int m = c0 / a.topk + tid; m < c1 / a.topk; m += blockDim.x) {
+            int c = 0;
+            for (int k = 0; k < a.topk; ++k) c += s_ids[m * a.topk + k - c0] >= 0 ? 1 : 0;
+            a.tok_cnt[m] = c;
+            if (c == 0) {   // no active pick: the token's output row is zero
+                for (int col = 0; col < a.H; ++col) {
+                    if (a.out_bf16 == 2) reinterpret_cast<float*>(a.out)[(long long)m * a.os + col] = 0.0f;
+                    else if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + col] = __float2bfloat16(0.0f);
+                    else reinterpret_cast<__half*>(a.out)[(long long)m * a.os + col] = __float2half(0.0f);
+                }
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
+    // entry bases: exclusive scan of ceil(count / kTokPerEnt) over experts
     const int e = tid;
     const int n = (e < a.E) ? cnt[e] : 0;
     const int ne = (n + kTokPerEnt - 1) / kTokPerEnt;
@@ -99,38 +115,205 @@ __device__ void route_prep_block(const DecodeArgs& a) {
     __syncthreads();
     const int base = (wid ? sh_warp2[wid - 1] : 0) + x - ne;
     if (tid == 0) a.n_ent[0] = sh_warp2[31];
-    if (n > 0) {
-        int j = 0;
-        for (int i = 0; i < npairs && j < n; ++i) {
-            if (a.ids[i] != e || !a.pick_act[i]) continue;
-            int en = base + j / kTokPerEnt, s = j % kTokPerEnt;
-            if (s == 0) {
-                a.ent_expert[en] = e;
-                a.ent_n[en] = min(kTokPerEnt, n - j);
-                a.ent_blob[en] = (long long)a.ptrs[e];
-                a.ent_k[en] = a.kinfo ? a.kinfo[e] : (a.K | (a.K << 4) | (a.K << 8));
-                for (int q = 0; q < kTokPerEnt; ++q) { a.ent_tok[en * kTokPerEnt + q] = 0; a.ent_pick[en * kTokPerEnt + q] = 0; }
-            }
-            a.ent_tok[en * kTokPerEnt + s] = i / a.topk;
-            a.ent_w[en * kTokPerEnt + s] = a.w[i];
-            a.ent_pick[en * kTokPerEnt + s] = i;
-            ++j;
+    // pass 2: every expert thread collects its picks in ascending index
+    int j = 0;
+    for (int c0 = 0; c0 < npairs; c0 += chunk) {
+        const int c1 = min(npairs, c0 + chunk);
+        __syncthreads();
+        for (int i = c0 + tid; i < c1; i += blockDim.x) {
+            s_ids[i - c0] = a.pick_act[i] ? a.ids[i] : -1;
+            s_w[i - c0] = a.w[i];
         }
-    }
-    for (int m = 0; m < a.M; ++m) {
-        if (a.tok_cnt[m] != 0) continue;
-        for (int c = tid; c < a.H; c += blockDim.x) {
-            if (a.out_bf16 == 2) reinterpret_cast<float*>(a.out)[(long long)m * a.os + c] = 0.0f;
-            else if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + c] = __float2bfloat16(0.0f);
-            else reinterpret_cast<__half*>(a.out)[(long long)m * a.os + c] = __float2half(0.0f);
+        __syncthreads();
+        if (n > 0 && j < n) {
+            for (int i = c0; i < c1 && j < n; ++i) {
+                if (s_ids[i - c0] != e) continue;
+                int en = base + j / kTokPerEnt, sl = j % kTokPerEnt;
+                if (sl == 0) {
+                    a.ent_expert[en] = e;
+                    a.ent_n[en] = min(kTokPerEnt, n - j);
+                    a.ent_blob[en] = (long long)a.ptrs[e];
+                    a.ent_k[en] = a.kinfo ? a.kinfo[e] : (a.K | (a.K << 4) | (a.K << 8));
+                    for (int q = 0; q < kTokPerEnt; ++q) { a.ent_tok[en * kTokPerEnt + q] = 0; a.ent_pick[en * kTokPerEnt + q] = 0; }
+                }
+                a.ent_tok[en * kTokPerEnt + sl] = i / a.topk;
+                a.ent_w[en * kTokPerEnt + sl] = s_w[i - c0];
+                a.ent_pick[en * kTokPerEnt + sl] = i;
+                ++j;
+            }
         }
     }
 }
 
-// Cached calls run the device cache step first (in place on ids / w), then the grouping.
+// Small batches (M <= kTokPerEnt tokens, at most 128 picks) in one warp, without block barriers: the same results as
+// ensure_block + route_prep_block when every pick is a hit or tier-masked (no cache miss, ids in range).  Returns
+// false, having written nothing, when that does not hold; the caller then runs the block path.
+__device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const DecodeArgs& a, int cached) {
+    constexpr int J = 4;   // picks per lane: i = lane + 32 j
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int np = a.M * a.topk, E = a.E;
+    const unsigned lt = (1u << lane) - 1u;
+    const int kpack = a.K | (a.K << 4) | (a.K << 8);
+    int id[J];
+    float wv[J];
+    bool val[J];
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        val[j] = i < np;
+        id[j] = val[j] ? a.ids[i] : 0;
+        wv[j] = val[j] ? a.w[i] : 0.0f;
+        bad |= val[j] && (id[j] < 0 || id[j] >= E);
+    }
+    if (__any_sync(FULL, bad)) return false;
+    const bool tier = cached && ea.ram_res != nullptr;
+    const int L = cached ? ea.layer : 0;
+    const int safe = tier ? ea.safe[L] : 0;
+    const int ring0 = tier ? ea.ring[0] : 0;
+    const int tick0 = cached ? ea.tick[0] : 0;
+    const int so_safe = tier ? ea.slot_of[L * E + safe] : -1;
+    int so[J], kv[J];
+    long long pt[J];
+    bool masked[J];
+    bool miss = false;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        so[j] = -1; kv[j] = kpack; pt[j] = 0; masked[j] = false;
+        if (val[j]) {
+            const int key = L * E + id[j];
+            so[j] = cached ? ea.slot_of[key] : 0;
+            const bool in_ram = tier ? ea.ram_res[key] != 0 : true;
+            pt[j] = (long long)a.ptrs[id[j]];
+            if (a.kinfo) kv[j] = a.kinfo[id[j]];
+            masked[j] = tier && so[j] < 0 && !in_ram;
+            miss |= cached && !masked[j] && so[j] < 0;
+            miss |= masked[j] && so_safe < 0;   // the safe expert itself would be a miss
+        }
+    }
+    if (__any_sync(FULL, miss)) return false;
+    if (cached) {
+        const long long pt_safe = tier ? (long long)a.ptrs[safe] : 0;
+        const int kv_safe = (tier && a.kinfo) ? a.kinfo[safe] : kpack;
+        // 1. tier mask in ascending pick index: ring log, pick -> (safe, 0)
+        int base = ring0;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const unsigned bm = __ballot_sync(FULL, masked[j]);
+            if (masked[j]) {
+                const int i = lane + 32 * j;
+                ea.ring[1 + ((base + __popc(bm & lt)) % ea.ring_cap)] = L * E + id[j];
+                ea.ids[i] = safe;
+                ea.w[i] = 0.0f;
+                id[j] = safe; wv[j] = 0.0f; so[j] = so_safe; pt[j] = pt_safe; kv[j] = kv_safe;
+            }
+            base += __popc(bm);
+        }
+        // 2.-4. tick; every used slot stamped with it unless pinned (T exceeds every unpinned stamp: a max)
+        const int T = tick0 + 1;
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            if (val[j] && so[j] >= 0) atomicMax(&ea.slot_last[so[j]], T);
+        if (lane == 0) {
+            if (tier) ea.ring[0] = base;
+            ea.tick[0] = T;
+            ea.fill_list[0] = 0;
+            if (ea.vict) ea.vict[0] = 0;
+        }
+    }
+    // grouping: one entry per distinct active expert (M <= kTokPerEnt: an expert has at most M picks), ascending id,
+    // its picks in ascending index
+    bool act[J];
+    int sl[J], cnt[J], en[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        act[j] = val[j] && !(a.skip_zero && wv[j] == 0.0f);
+        sl[j] = 0; cnt[j] = 0; en[j] = 0;
+    }
+#pragma unroll
+    for (int qj = 0; qj < J; ++qj) {
+        if (qj * 32 >= np) break;
+        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
+            const int eq = __shfl_sync(FULL, id[qj], ql);
+            const int aq = __shfl_sync(FULL, (int)act[qj], ql);
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                if (act[j] && aq && eq == id[j]) {
+                    ++cnt[j];
+                    if (qj * 32 + ql < lane + 32 * j) ++sl[j];
+                }
+        }
+    }
+    int ndist = 0;
+#pragma unroll
+    for (int qj = 0; qj < J; ++qj) {
+        if (qj * 32 >= np) break;
+        const bool first_q = act[qj] && sl[qj] == 0;
+        ndist += __popc(__ballot_sync(FULL, first_q));
+        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
+            const int eq = __shfl_sync(FULL, id[qj], ql);
+            const int fq = __shfl_sync(FULL, (int)first_q, ql);
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                if (fq && eq < id[j]) ++en[j];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        if (val[j]) a.pick_act[i] = act[j] ? 1 : 0;
+        if (!act[j]) continue;
+        const int e8 = en[j] * kTokPerEnt;
+        if (sl[j] == 0) {
+            a.ent_expert[en[j]] = id[j];
+            a.ent_n[en[j]] = cnt[j];
+            a.ent_blob[en[j]] = pt[j];
+            a.ent_k[en[j]] = kv[j];
+            for (int q = cnt[j]; q < kTokPerEnt; ++q) { a.ent_tok[e8 + q] = 0; a.ent_pick[e8 + q] = 0; }
+        }
+        a.ent_tok[e8 + sl[j]] = i / a.topk;
+        a.ent_w[e8 + sl[j]] = wv[j];
+        a.ent_pick[e8 + sl[j]] = i;
+    }
+    if (lane == 0) a.n_ent[0] = ndist;
+    for (int m = 0; m < a.M; ++m) {
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < J; ++j) c += (act[j] && (lane + 32 * j) / a.topk == m) ? 1 : 0;
+        c = __reduce_add_sync(FULL, (unsigned)c);
+        if (lane == 0) a.tok_cnt[m] = c;
+        if (c == 0) {   // no active pick: the token's output row is zero
+            for (int col = lane; col < a.H; col += 32) {
+                if (a.out_bf16 == 2) reinterpret_cast<float*>(a.out)[(long long)m * a.os + col] = 0.0f;
+                else if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + col] = __float2bfloat16(0.0f);
+                else reinterpret_cast<__half*>(a.out)[(long long)m * a.os + col] = __float2half(0.0f);
+            }
+        }
+    }
+    return true;
+}
+
+// Cached calls run the device cache step first (in place on ids / w), then the grouping.  Small batches try the
+// one-warp path first (the other warps zero the arrival counters meanwhile).
 __global__ void __launch_bounds__(1024) prep_kernel(EnsureArgs ea, DecodeArgs da, int cached) {
+    __shared__ int sh_fast;
     pdl_wait();
     pdl_trigger();
+    if (da.M <= kTokPerEnt && da.M * da.topk <= 128 && !(cached && ea.prefetch)) {
+        if (threadIdx.x < 32) {
+            const bool ok = prep_fast_warp(ea, da, cached);
+            if (threadIdx.x == 0) sh_fast = ok ? 1 : 0;
+        } else {
+            const int nbI = da.I / 128, nbH = da.H / 128;
+            for (int i = threadIdx.x - 32; i < da.maxent * nbI; i += blockDim.x - 32) da.cnt_gu[i] = 0;
+            for (int i = threadIdx.x - 32; i < da.maxent * nbH; i += blockDim.x - 32) da.cnt_d[i] = 0;
+            for (int i = threadIdx.x - 32; i < da.M * nbH; i += blockDim.x - 32) da.cnt_c[i] = 0;
+            if (threadIdx.x == 32) da.blocks_done[0] = 0;
+        }
+        __syncthreads();
+        if (sh_fast) return;
+    }
     if (cached) {
         ensure_block(ea);
         __syncthreads();
@@ -143,7 +326,7 @@ __global__ void __launch_bounds__(1024) prep_kernel(EnsureArgs ea, DecodeArgs da
 // L2-only), kStages rows ahead of the decode.  A strip row is 2 PLANAR4 groups; in SMEM each plane of a group is
 // padded to 4G + 8 words (D > 1), so the two words a lane reads per tile -- word (tile j, period g, plane i) at
 // i*PS + j*G + g -- fall in distinct banks across the warp.  Unit metadata is loaded one unit ahead.
-constexpr int kStages = 5;
+constexpr int kStages = 4;   // divides the 8 rows of a unit: ring slots are compile-time per row
 
 __device__ __forceinline__ void cp_async16(uint32_t* smem, const void* gmem) {
     unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -203,6 +386,8 @@ struct StreamCfg {
 struct UMeta {
     int valid, ent, f0, f1, f2, K, kv, ntok, tok, pick;   // f0..f2: (proj, nb, kb) gate-up; (nbh, kbi, -) down
     const uint8_t* blob;
+    const uint32_t* src;   // first word of the unit's strip (row 0)
+    int rs;                // words between strip rows
 };
 
 template <int PHASE>
@@ -212,6 +397,7 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
     m.valid = u < n_units;
     if (!m.valid) {
         m.ent = 0; m.f0 = m.f1 = m.f2 = 0; m.K = 3; m.kv = 0; m.ntok = 0; m.tok = 0; m.pick = 0; m.blob = nullptr;
+        m.src = nullptr; m.rs = 0;
         return m;
     }
     if (PHASE == 0) {
@@ -230,36 +416,37 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
     m.K = PHASE == 0 ? (m.f0 ? (m.kv >> 4) & 15 : m.kv & 15) : (m.kv >> 8) & 15;
     m.tok = lane < kTokPerEnt ? __ldcg(a.ent_tok + m.ent * kTokPerEnt + lane) : 0;
     m.pick = lane < kTokPerEnt ? __ldcg(a.ent_pick + m.ent * kTokPerEnt + lane) : 0;
+    const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(m.blob);
+    if (PHASE == 0) {
+        m.rs = (int)gm.gu_row_words();
+        m.src = words + (size_t)(m.f2 * 8) * m.rs + (m.f0 ? (size_t)(a.I / 16) * 8 * gm.Kg : 0) + (size_t)(m.f1 * 2) * 4 * 8 * m.K;
+    } else {
+        m.rs = (int)gm.d_row_words();
+        m.src = words + gm.gu_words() + (size_t)(m.f1 * 8) * m.rs + (size_t)(m.f0 * 2) * 4 * 8 * m.K;
+    }
     return m;
 }
 
-// Issue the cp.async copies of stream row r of unit m into `stage` (and, for gate-up row 0, its side slot).
+// Issue the cp.async copies of stream row r of unit m into `stage` (and, for gate-up row 0, its side slot: the
+// unit's suh block and the x blocks of its tokens).
 template <int K, int PHASE>
 __device__ __forceinline__ void issue_row(const DecodeArgs& a, const UMeta& m, int r, uint32_t* stage, uint32_t* side,
                                           const LaneK<K>& lk) {
     using R = Ring<K>;
     const int lane = threadIdx.x & 31;
-    const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
-    const uint32_t* src;
-    if (PHASE == 0) {
-        const size_t proj_off = m.f0 ? (size_t)(a.I / 16) * 8 * gm.Kg : 0;
-        src = reinterpret_cast<const uint32_t*>(m.blob) + (size_t)(m.f2 * 8 + r) * gm.gu_row_words() + proj_off +
-              (size_t)(m.f1 * 2) * 4 * R::W;
-    } else {
-        src = reinterpret_cast<const uint32_t*>(m.blob) + gm.gu_words() + (size_t)(m.f1 * 8 + r) * gm.d_row_words() +
-              (size_t)(m.f0 * 2) * 4 * R::W;
-    }
+    const uint32_t* src = m.src + (size_t)r * m.rs;
 #pragma unroll
     for (int q = 0; q < 3; ++q)
         if (lane + 32 * q < R::CHUNKS) cp_async16(stage + lk.dst[q], src + 4 * (lane + 32 * q));
     if (PHASE == 0 && r == 0) {
+        const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
         if (lane < 16)
             cp_async16(side + lane * 4, m.blob + gm.off_suh_g() + (size_t)m.f0 * a.H * 2 + (size_t)m.f2 * 256 + lane * 16);
-#pragma unroll
-        for (int c = lane; c < 16 * kTokPerEnt; c += 32) {   // uniform trip count: the shuffle sees every lane
-            int t = c >> 4, j = c & 15;
-            int tk = __shfl_sync(0xffffffffu, m.tok, t);
-            if (t < m.ntok)
+        for (int c0 = 0; c0 < 16 * m.ntok; c0 += 32) {   // uniform trip count: the shuffle sees every lane
+            const int c = c0 + lane, t = (c >> 4) & 7, j = c & 15;
+            const int tk = __shfl_sync(0xffffffffu, m.tok, t);
+            if (c < 16 * m.ntok)
                 cp_async16(side + 64 + t * 64 + j * 4,
                            reinterpret_cast<const uint8_t*>(a.x) + ((size_t)tk * a.xs + (size_t)m.f2 * 128) * 2 + j * 16);
         }
@@ -288,9 +475,9 @@ __device__ __forceinline__ void unit_xh(const DecodeArgs& a, const UMeta& m, con
     float su[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) su[j] = __half2float(suh[4 * lane + j]);
-    for (int t = 0; t < kTokPerEnt; ++t) {
+    for (int t = 0; t < m.ntok; ++t) {   // columns of padding tokens are never read back
         uint2 o = make_uint2(0u, 0u);
-        if (t < m.ntok) {
+        {
             const uint16_t* xr = reinterpret_cast<const uint16_t*>(side + 64 + t * 64);
             float v[4];
 #pragma unroll
@@ -328,132 +515,93 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, long long o, cons
     }
 }
 
-// Unit epilogues: split-K partials, then (last arriver only) the column-block epilogue.
-__device__ void gu_epilogue(const DecodeArgs& a, const UMeta& m, float acc[8][4]) {
+// Item epilogues (one warp per token t of the entry; lane holds columns 4 lane .. 4 lane + 3 of the 128-block).
+// Gate-up (:239-256): g = fp16(FWHT(g) r svh_g), u likewise, a = fp16(SiLU(g) u), a = fp16(a suh_d),
+// abuf = fp16(FWHT(a) r).
+// The lane's scale vectors (svh_g, svh_u, suh_d: 4 fp16 each at columns 4 lane..) and the token's pick index, loaded
+// before the item's decode so that the epilogue waits on no global load.
+struct GuEpi {
+    uint2 svg, svu, sud;
+    int pick;
+};
+__device__ __forceinline__ GuEpi gu_epi_load(const DecodeArgs& a, int ent, int nb, int t) {
     const int lane = threadIdx.x & 31;
-    const int nKB = a.H / 128, nbI = a.I / 128;
-    const int proj = m.f0, nb = m.f1, kb = m.f2;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        int t = 2 * (lane & 3) + q;
-        int pick = __shfl_sync(0xffffffffu, m.pick, t);
-        if (t < m.ntok) {
-            float* dst = a.part_gu + ((size_t)(pick * 2 + proj) * nKB + kb) * a.I + nb * 128 + (lane >> 2);
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                __stcg(dst + jj * 16, acc[jj][q]);
-                __stcg(dst + jj * 16 + 8, acc[jj][2 + q]);
-            }
-        }
-    }
-    __syncwarp();
-    __threadfence();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&a.cnt_gu[m.ent * nbI + nb], 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != 2 * nKB - 1) return;
-    __threadfence();
-    const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
-    const __half* svg = reinterpret_cast<const __half*>(m.blob + gm.off_svh_g()) + nb * 128 + 4 * lane;
-    const __half* svu = reinterpret_cast<const __half*>(m.blob + gm.off_svh_u()) + nb * 128 + 4 * lane;
-    const __half* sud = reinterpret_cast<const __half*>(m.blob + gm.off_suh_d()) + nb * 128 + 4 * lane;
-    for (int t = 0; t < m.ntok; ++t) {
-        int pick = __shfl_sync(0xffffffffu, m.pick, t);
-        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* pg = a.part_gu + (size_t)(pick * 2 + 0) * nKB * a.I + nb * 128 + 4 * lane;
-        const float* pu = a.part_gu + (size_t)(pick * 2 + 1) * nKB * a.I + nb * 128 + 4 * lane;
-#pragma unroll 8
-        for (int k = 0; k < nKB; ++k) {
-            float4 vg = __ldcg(reinterpret_cast<const float4*>(pg + (size_t)k * a.I));
-            float4 vu = __ldcg(reinterpret_cast<const float4*>(pu + (size_t)k * a.I));
-            g[0] += vg.x; g[1] += vg.y; g[2] += vg.z; g[3] += vg.w;
-            u[0] += vu.x; u[1] += vu.y; u[2] += vu.z; u[3] += vu.w;
-        }
-        fwht128_warp(g, lane);
-        fwht128_warp(u, lane);
-        float act[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float gv = rn16(g[j] * kRsqrt128 * __half2float(svg[j]));
-            float uv = rn16(u[j] * kRsqrt128 * __half2float(svu[j]));
-            float sl = gv / (1.0f + expf(-gv)) * uv;
-            sl = rn16(sl);
-            act[j] = rn16(sl * __half2float(sud[j]));
-        }
-        fwht128_warp(act, lane);
-        __half2 h0 = __floats2half2_rn(act[0] * kRsqrt128, act[1] * kRsqrt128);
-        __half2 h1 = __floats2half2_rn(act[2] * kRsqrt128, act[3] * kRsqrt128);
-        uint2 o;
-        o.x = *reinterpret_cast<uint32_t*>(&h0);
-        o.y = *reinterpret_cast<uint32_t*>(&h1);
-        __stcg(reinterpret_cast<uint2*>(a.abuf + (size_t)pick * a.I + nb * 128 + 4 * lane), o);
-    }
-    if (lane == 0) a.cnt_gu[m.ent * nbI + nb] = 0;
+    const int kv = __ldcg(a.ent_k + ent);
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + ent));
+    const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
+    GuEpi q;
+    q.svg = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_g()) + nb * 128 + 4 * lane));
+    q.svu = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_u()) + nb * 128 + 4 * lane));
+    q.sud = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_suh_d()) + nb * 128 + 4 * lane));
+    q.pick = __ldcg(a.ent_pick + ent * kTokPerEnt + t);
+    return q;
 }
 
-__device__ void dn_epilogue(const DecodeArgs& a, const UMeta& m, float acc[8][4]) {
+__device__ __forceinline__ void gu_token_epilogue(const DecodeArgs& a, const GuEpi& q, int nb, const float g_in[4],
+                                                  const float u_in[4]) {
     const int lane = threadIdx.x & 31;
-    const int nKBd = a.I / 128, nbH = a.H / 128;
-    const int nbh = m.f0, kbi = m.f1;
+    const __half* svg = reinterpret_cast<const __half*>(&q.svg);
+    const __half* svu = reinterpret_cast<const __half*>(&q.svu);
+    const __half* sud = reinterpret_cast<const __half*>(&q.sud);
+    const int pick = q.pick;
+    float g[4] = {g_in[0], g_in[1], g_in[2], g_in[3]}, u[4] = {u_in[0], u_in[1], u_in[2], u_in[3]};
+    fwht128_warp(g, lane);
+    fwht128_warp(u, lane);
+    float act[4];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        int t = 2 * (lane & 3) + q;
-        int pick = __shfl_sync(0xffffffffu, m.pick, t);
-        if (t < m.ntok) {
-            float* dst = a.part_d + ((size_t)pick * nKBd + kbi) * a.H + nbh * 128 + (lane >> 2);
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                __stcg(dst + jj * 16, acc[jj][q]);
-                __stcg(dst + jj * 16 + 8, acc[jj][2 + q]);
-            }
-        }
+    for (int j = 0; j < 4; ++j) {
+        float gv = rn16(g[j] * kRsqrt128 * __half2float(svg[j]));
+        float uv = rn16(u[j] * kRsqrt128 * __half2float(svu[j]));
+        float sl = gv / (1.0f + expf(-gv)) * uv;
+        sl = rn16(sl);
+        act[j] = rn16(sl * __half2float(sud[j]));
     }
+    fwht128_warp(act, lane);
+    __half2 h0 = __floats2half2_rn(act[0] * kRsqrt128, act[1] * kRsqrt128);
+    __half2 h1 = __floats2half2_rn(act[2] * kRsqrt128, act[3] * kRsqrt128);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    __stcg(reinterpret_cast<uint2*>(a.abuf + (size_t)pick * a.I + nb * 128 + 4 * lane), o);
+}
+
+// Down (:355-364): y = FWHT(v) (r w) svh_d (fp32); then the combine (:387-394) of the token's 128-block by the last
+// of its active picks to finish: out[m] = sum_k y[m,k] in fixed k order.
+__device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, int nbh, int t, const float v_in[4]) {
+    const int lane = threadIdx.x & 31;
+    const int nbH = a.H / 128;
+    const int kv = __ldcg(a.ent_k + ent);
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + ent));
+    const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
+    const __half* svd = reinterpret_cast<const __half*>(blob + gm.off_svh_d()) + nbh * 128 + 4 * lane;
+    const int pick = __ldcg(a.ent_pick + ent * kTokPerEnt + t);
+    const float wt = __ldcg(a.ent_w + ent * kTokPerEnt + t);
+    float v[4] = {v_in[0], v_in[1], v_in[2], v_in[3]};
+    fwht128_warp(v, lane);
+    float4 yv;
+    yv.x = v[0] * (kRsqrt128 * wt) * __half2float(svd[0]);
+    yv.y = v[1] * (kRsqrt128 * wt) * __half2float(svd[1]);
+    yv.z = v[2] * (kRsqrt128 * wt) * __half2float(svd[2]);
+    yv.w = v[3] * (kRsqrt128 * wt) * __half2float(svd[3]);
+    __stcg(reinterpret_cast<float4*>(a.y + (size_t)pick * a.H + nbh * 128 + 4 * lane), yv);
     __syncwarp();
     __threadfence();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&a.cnt_d[m.ent * nbH + nbh], 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != nKBd - 1) return;
-    __threadfence();
-    const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
-    const __half* svd = reinterpret_cast<const __half*>(m.blob + gm.off_svh_d()) + nbh * 128 + 4 * lane;
-    for (int t = 0; t < m.ntok; ++t) {
-        int pick = __shfl_sync(0xffffffffu, m.pick, t);
-        float wt = __ldcg(a.ent_w + m.ent * kTokPerEnt + t);
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* pp = a.part_d + (size_t)pick * nKBd * a.H + nbh * 128 + 4 * lane;
-#pragma unroll 6
-        for (int k = 0; k < nKBd; ++k) {
-            float4 pv = __ldcg(reinterpret_cast<const float4*>(pp + (size_t)k * a.H));
-            v[0] += pv.x; v[1] += pv.y; v[2] += pv.z; v[3] += pv.w;
-        }
-        fwht128_warp(v, lane);
-        float4 yv;
-        yv.x = v[0] * (kRsqrt128 * wt) * __half2float(svd[0]);
-        yv.y = v[1] * (kRsqrt128 * wt) * __half2float(svd[1]);
-        yv.z = v[2] * (kRsqrt128 * wt) * __half2float(svd[2]);
-        yv.w = v[3] * (kRsqrt128 * wt) * __half2float(svd[3]);
-        __stcg(reinterpret_cast<float4*>(a.y + (size_t)pick * a.H + nbh * 128 + 4 * lane), yv);
-        __syncwarp();
+    const int mt = pick / a.topk;
+    int oc = 0;
+    if (lane == 0) oc = atomicAdd(&a.cnt_c[mt * nbH + nbh], 1);
+    oc = __shfl_sync(0xffffffffu, oc, 0);
+    if (oc == __ldcg(a.tok_cnt + mt) - 1) {
         __threadfence();
-        int mt = pick / a.topk;
-        int oc = 0;
-        if (lane == 0) oc = atomicAdd(&a.cnt_c[mt * nbH + nbh], 1);
-        oc = __shfl_sync(0xffffffffu, oc, 0);
-        if (oc == __ldcg(a.tok_cnt + mt) - 1) {
-            __threadfence();
-            float s[4] = {0.f, 0.f, 0.f, 0.f};
+        float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-            for (int k = 0; k < a.topk; ++k) {
-                int p = mt * a.topk + k;
-                if (!__ldcg(a.pick_act + p)) continue;
-                float4 q4 = __ldcg(reinterpret_cast<const float4*>(a.y + (size_t)p * a.H + nbh * 128 + 4 * lane));
-                s[0] += q4.x; s[1] += q4.y; s[2] += q4.z; s[3] += q4.w;
-            }
-            store_out(a, (long long)mt * a.os + nbh * 128 + 4 * lane, s);
+        for (int k = 0; k < a.topk; ++k) {
+            int pp = mt * a.topk + k;
+            if (!__ldcg(a.pick_act + pp)) continue;
+            float4 q4 = __ldcg(reinterpret_cast<const float4*>(a.y + (size_t)pp * a.H + nbh * 128 + 4 * lane));
+            sm[0] += q4.x; sm[1] += q4.y; sm[2] += q4.z; sm[3] += q4.w;
         }
+        store_out(a, (long long)mt * a.os + nbh * 128 + 4 * lane, sm);
     }
-    if (lane == 0) a.cnt_d[m.ent * nbH + nbh] = 0;
 }
 
 template <int K, int PHASE>
@@ -515,107 +663,241 @@ __device__ __forceinline__ void copy_fills(const DecodeArgs& a) {
     }
 }
 
-// PHASE 0: gate|up units (entry, proj, nb, kb); PHASE 1: down units (entry, nbh, kbi).  Units are interleaved over
-// the grid block-major (unit u -> block u % grid), so every SM gets an equal share; each warp runs one continuous row
-// stream over its units.
+// Stream a warp's units (unit ids u0, u0 + ustep, ... : nu of them, all of one item) row by row through the warp's
+// SMEM ring (kStages rows in flight, rows unrolled so every ring slot is fixed) and accumulate W^T B over all of them
+// into acc.  PHASE 1 waits for the previous kernel (wait_pdl) after the ring prologue is issued, before its first
+// read of abuf.
 template <int KFIX, int PHASE>
-__global__ void __launch_bounds__(256, 2) stream_kernel(DecodeArgs a) {
+__device__ __forceinline__ void run_units(const DecodeArgs& a, int u0, int ustep, int nu, uint32_t* ring, uint32_t* side,
+                                          __half* xs, float acc[8][4], const LaneK<KFIX ? KFIX : 3>& lkf, bool wait_pdl) {
     using C = StreamCfg<KFIX, PHASE>;
+    static_assert(8 % kStages == 0, "ring slots must repeat every unit");
+    const int lane = threadIdx.x & 31;
+    auto meta = [&](int i) { return load_meta<PHASE>(a, u0 + i * ustep, i < nu ? 0x7FFFFFFF : 0); };
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) acc[jj][0] = acc[jj][1] = acc[jj][2] = acc[jj][3] = 0.0f;
+    UMeta mc = meta(0);
+    if (mc.valid) {
+#pragma unroll
+        for (int r = 0; r < kStages - 1; ++r) {
+            issue_any<KFIX, PHASE>(a, mc, r, ring + r * C::STAGE, side, lkf);
+            cp_commit();
+        }
+    }
+    if (PHASE == 1 && wait_pdl) {
+        pdl_wait();
+        pdl_trigger();
+    }
+    const int tk = lane >> 2, kq = 2 * (lane & 3);
+    auto load_b = [&](const UMeta& m, int r, uint32_t& b0, uint32_t& b1) {
+        const int pk = __shfl_sync(0xffffffffu, m.pick, tk);
+        if (tk < m.ntok) {
+            const __half* ar = a.abuf + (size_t)pk * a.I + m.f1 * 128 + r * 16 + kq;
+            b0 = __ldcg(reinterpret_cast<const unsigned int*>(ar));
+            b1 = __ldcg(reinterpret_cast<const unsigned int*>(ar + 8));
+        } else {
+            b0 = b1 = 0u;
+        }
+    };
+    uint32_t nb0 = 0, nb1 = 0;   // down: B operand of the next row, loaded one row ahead
+    if (PHASE == 1 && mc.valid) load_b(mc, 0, nb0, nb1);
+    for (int i = 0; i < nu; ++i) {
+        const UMeta mn = meta(i + 1);
+        uint32_t* sd = side + (i & 1) * kSideWords;
+        uint32_t* sdn = side + ((i + 1) & 1) * kSideWords;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            constexpr int L = kStages - 1;
+            const int rr = r + L;   // row issued now: of this unit, or (rr >= 8) of the next one
+            if (rr < 8) issue_any<KFIX, PHASE>(a, mc, rr, ring + (rr % kStages) * C::STAGE, sd, lkf);
+            else if (mn.valid) issue_any<KFIX, PHASE>(a, mn, rr - 8, ring + (rr % kStages) * C::STAGE, sdn, lkf);
+            cp_commit();
+            cp_wait<kStages - 1>();
+            __syncwarp();
+            const uint32_t* stage = ring + (r % kStages) * C::STAGE;
+            if (PHASE == 0 && r == 0) unit_xh(a, mc, sd, xs);
+            uint32_t b0, b1;
+            if (PHASE == 0) {
+                b0 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq);
+                b1 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq + 8);
+            } else {
+                b0 = nb0;
+                b1 = nb1;
+                if (r < 7) load_b(mc, r + 1, nb0, nb1);
+                else if (mn.valid) load_b(mn, 0, nb0, nb1);
+            }
+            consume_any<KFIX>(mc.K, stage, b0, b1, acc, lkf);
+            __syncwarp();
+        }
+        mc = mn;
+    }
+    cp_wait<0>();
+    __syncwarp();
+}
+
+// acc (mma accumulator layout: acc[jj][q] = column jj*16 + lane/4 (+8 for q >= 2), token 2(lane%4) + (q & 1)) ->
+// red[token][column] (128 columns x kTokPerEnt tokens).
+__device__ __forceinline__ void acc_to_smem(const float acc[8][4], float* red) {
+    const int lane = threadIdx.x & 31;
+    const int c0 = lane >> 2, t0 = 2 * (lane & 3);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+        red[(t0 + 0) * 128 + jj * 16 + c0] = acc[jj][0];
+        red[(t0 + 1) * 128 + jj * 16 + c0] = acc[jj][1];
+        red[(t0 + 0) * 128 + jj * 16 + c0 + 8] = acc[jj][2];
+        red[(t0 + 1) * 128 + jj * 16 + c0 + 8] = acc[jj][3];
+    }
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+// Cluster-wide barrier (release / acquire): every CTA of the cluster reaches it the same number of times.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// Load from the shared memory of CTA `rank` of this cluster at the address this CTA uses for `p`.
+__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+    uint32_t la = (uint32_t)__cvta_generic_to_shared(p), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+// Gate-up: a cluster of cs CTAs (4, or 2 when H/128 is odd) per item (entry, 128-column block of I).  The item's
+// 2 H/128 units (proj, 128-row k-block) are split evenly: CTA rank r takes units of projection r / (cs/2), k-blocks
+// (r % (cs/2)) * upc + w + 8 j for its warp w.  Each CTA sums its warps' accumulators in shared memory (fixed
+// order); rank 0 adds the CTAs' sums of each projection (fixed rank order, read over DSMEM) and runs the epilogue,
+// one warp per token.  Items are dealt to clusters round-robin; no global partials, no atomics.
+template <int KFIX>
+__global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
+    using C = StreamCfg<KFIX, 0>;
     extern __shared__ __align__(16) uint32_t smem[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     uint32_t* ring = smem + wid * C::WARP_WORDS;
-    uint32_t* side = ring + kStages * C::STAGE;                    // gate-up: 2 side slots
-    __half* xs = reinterpret_cast<__half*>(side + 2 * kSideWords);  // gate-up: xh [8][kXsStride]
+    uint32_t* side = ring + kStages * C::STAGE;
+    __half* xs = reinterpret_cast<__half*>(side + 2 * kSideWords);
+    float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS);   // CTA sum [token][128]
     LaneK<KFIX ? KFIX : 3> lkf;
     lkf.init(lane);
-    const int G = gridDim.x;
-    auto unit_of = [&](int i) { return (int)blockIdx.x + (wid + 8 * i) * G; };
-    // Entries come from the prep kernel (two launches back for the down phase): the down phase loads its first unit
-    // and starts streaming weights before waiting for gate-up, whose abuf it needs only for its B operands.
-    if (PHASE == 0) pdl_wait();
-    const int n_ent = __ldcg(a.n_ent);
-    const int n_units = PHASE == 0 ? n_ent * 2 * (a.I / 128) * (a.H / 128) : n_ent * (a.H / 128) * (a.I / 128);
-    UMeta mc = load_meta<PHASE>(a, unit_of(0), n_units);
-    UMeta mn = load_meta<PHASE>(a, unit_of(1), n_units);
-    int ic = 0;
-    auto issue = [&](int pos) {
-        int i = pos >> 3, r = pos & 7;
-        const UMeta& m = (i == ic) ? mc : mn;
-        if (i <= ic + 1) issue_any<KFIX, PHASE>(a, m, r, ring + (pos % kStages) * C::STAGE, side + (i & 1) * kSideWords, lkf);
-        cp_commit();
-    };
-    if (mc.valid) {
-#pragma unroll
-        for (int p = 0; p < kStages - 1; ++p) issue(p);
-    }
-    if (PHASE == 1) pdl_wait();
+    const int cs = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
+    const int cid = (int)blockIdx.x / cs, ncl = (int)gridDim.x / cs;
+    pdl_wait();
     pdl_trigger();
-    if (PHASE == 0) copy_fills(a);
-    const int tk = lane >> 2, kq = 2 * (lane & 3);
-    float acc[8][4];
-    uint32_t nb0 = 0, nb1 = 0;   // down: B operand of the next row, loaded one row ahead
-    auto load_b = [&](const UMeta& m, int r) {
-        int pk = __shfl_sync(0xffffffffu, m.pick, tk);
-        if (tk < m.ntok) {
-            const __half* ar = a.abuf + (size_t)pk * a.I + m.f1 * 128 + r * 16 + kq;
-            nb0 = __ldcg(reinterpret_cast<const unsigned int*>(ar));
-            nb1 = __ldcg(reinterpret_cast<const unsigned int*>(ar + 8));
-        } else {
-            nb0 = nb1 = 0u;
-        }
-    };
-    if (PHASE == 1 && mc.valid) load_b(mc, 0);
-    for (int pos = 0; mc.valid; ++pos) {
-        const int i = pos >> 3, r = pos & 7;
-        if (r == 0 && i > 0) {
-            mc = mn;
-            ic = i;
-            if (!mc.valid) break;
-            mn = load_meta<PHASE>(a, unit_of(i + 1), n_units);
-        }
-        issue(pos + kStages - 1);
-        cp_wait<kStages - 1>();
-        __syncwarp();
-        const uint32_t* stage = ring + (pos % kStages) * C::STAGE;
-        if (r == 0) {
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[jj][0] = acc[jj][1] = acc[jj][2] = acc[jj][3] = 0.0f;
-            if (PHASE == 0) unit_xh(a, mc, side + (i & 1) * kSideWords, xs);
-        }
-        uint32_t b0, b1;
-        if (PHASE == 0) {
-            b0 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq);
-            b1 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq + 8);
-        } else {
-            b0 = nb0;
-            b1 = nb1;
-            if (r < 7) load_b(mc, r + 1);
-            else if (mn.valid) load_b(mn, 0);
-        }
-        consume_any<KFIX>(mc.K, stage, b0, b1, acc, lkf);
-        __syncwarp();
-        if (r == 7) {
-            if (PHASE == 0) gu_epilogue(a, mc, acc);
-            else dn_epilogue(a, mc, acc);
-        }
-    }
-    cp_wait<0>();
-    if (PHASE == 1) {
-        // the last block to finish commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386)
+    const int n_ent = __ldcg(a.n_ent);
+    const int nKB = a.H / 128, nbI = a.I / 128;
+    const int n_items = n_ent * nbI;
+    const int half = cs / 2, upc = nKB / half;     // units per CTA, all of one projection
+    const int proj = rank / half, kb0 = (rank % half) * upc;
+    for (int item = cid; item < n_items; item += ncl) {
+        const int ent = item / nbI, nb = item % nbI;
+        const int nu = upc > wid ? (upc - wid + 7) / 8 : 0;
+        const int u0 = ((ent * 2 + proj) * nbI + nb) * nKB + kb0 + wid;
+        GuEpi epi{};
+        if (rank == 0 && wid < __ldcg(a.ent_n + ent)) epi = gu_epi_load(a, ent, nb, wid);
+        float acc[8][4];
+        run_units<KFIX, 0>(a, u0, 8, nu, ring, side, xs, acc, lkf, false);
+        float* red = reinterpret_cast<float*>(ring);   // the warp's ring, side and xs are free now
+        acc_to_smem(acc, red);
         __syncthreads();
-        if (threadIdx.x == 0 && a.fill_list) {
-            __threadfence();
-            int old = atomicAdd(a.blocks_done, 1);
-            if (old == (int)gridDim.x - 1) {
-                __threadfence();
-                const int nf = __ldcg(a.fill_list);
-                for (int q = 0; q < nf; ++q) {
-                    int e = __ldcg(a.fill_list + 1 + q);
-                    a.ptrs[e] = __ldcg(a.fill + e);
-                    a.fill[e] = 0;
+        for (int q = threadIdx.x; q < kTokPerEnt * 128; q += 256) {
+            float sm = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) sm += reinterpret_cast<const float*>(smem + w * C::WARP_WORDS)[q];
+            part[q] = sm;
+        }
+        cluster_sync_all();
+        if (rank == 0) {
+            const int ntok = __ldcg(a.ent_n + ent);
+            if (wid < ntok) {
+                float g[4], u[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float* pe = part + wid * 128 + 4 * lane + j;
+                    float gs = 0.0f, us = 0.0f;
+                    for (int r = 0; r < half; ++r) gs += ld_dsmem(pe, r);
+                    for (int r = half; r < cs; ++r) us += ld_dsmem(pe, r);
+                    g[j] = gs;
+                    u[j] = us;
                 }
-                a.blocks_done[0] = 0;
+                gu_token_epilogue(a, epi, nb, g, u);
             }
+        }
+        cluster_sync_all();   // rank 0 has read every CTA's sums before they are overwritten or the CTAs exit
+    }
+    // cache fills are read by no kernel of this call (picks of a filled expert read its host copy until the commit
+    // at the end of the down phase): copied after the items, off the decode's critical path
+    copy_fills(a);
+}
+
+// Down: one CTA per item (entry, 128-column block of H); warp w takes the k-blocks w + 8 j of the I/128 units.  The
+// first item's weight rows are issued before the wait for the gate-up kernel (only abuf depends on it).
+template <int KFIX>
+__global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
+    using C = StreamCfg<KFIX, 1>;
+    extern __shared__ __align__(16) uint32_t smem[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint32_t* ring = smem + wid * C::WARP_WORDS;
+    float* red = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + wid * kTokPerEnt * 128;
+    float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + 8 * kTokPerEnt * 128;
+    LaneK<KFIX ? KFIX : 3> lkf;
+    lkf.init(lane);
+    const int n_ent = __ldcg(a.n_ent);   // prep finished before the gate-up kernel could let this one start
+    const int nKBd = a.I / 128, nbH = a.H / 128;
+    const int n_items = n_ent * nbH;
+    bool first = true;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int ent = item / nbH, nbh = item % nbH;
+        const int nu = nKBd > wid ? (nKBd - wid + 7) / 8 : 0;
+        const int u0 = (ent * nbH + nbh) * nKBd + wid;
+        float acc[8][4];
+        run_units<KFIX, 1>(a, u0, 8, nu, ring, nullptr, nullptr, acc, lkf, first);
+        first = false;
+        acc_to_smem(acc, red);
+        __syncthreads();
+        for (int q = threadIdx.x; q < kTokPerEnt * 128; q += 256) {
+            float sm = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) sm += reinterpret_cast<const float*>(smem + 8 * C::WARP_WORDS)[w * kTokPerEnt * 128 + q];
+            part[q] = sm;
+        }
+        __syncthreads();
+        const int ntok = __ldcg(a.ent_n + ent);
+        if (wid < ntok) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = part[wid * 128 + 4 * lane + j];
+            dn_token_epilogue(a, ent, nbh, wid, v);
+        }
+        __syncthreads();
+    }
+    if (first) {   // no item: still order this block after the gate-up kernel
+        pdl_wait();
+        pdl_trigger();
+    }
+    // the last block to finish commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386)
+    __syncthreads();
+    if (threadIdx.x == 0 && a.fill_list) {
+        __threadfence();
+        int old = atomicAdd(a.blocks_done, 1);
+        if (old == (int)gridDim.x - 1) {
+            __threadfence();
+            const int nf = __ldcg(a.fill_list);
+            for (int q = 0; q < nf; ++q) {
+                int e = __ldcg(a.fill_list + 1 + q);
+                a.ptrs[e] = __ldcg(a.fill + e);
+                a.fill[e] = 0;
+            }
+            a.blocks_done[0] = 0;
         }
     }
 }
@@ -647,17 +929,50 @@ static WsLayout ws_layout(int M, int topk, int H, int I) {
     return L;
 }
 
-template <int KFIX, int PHASE>
-static int launch_stream(const DecodeArgs& a, int grid, cudaStream_t s) {
-    using C = StreamCfg<KFIX, PHASE>;
-    static bool attr_set = false;   // per instantiation; the attribute is per function, set once per process
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(stream_kernel<KFIX, PHASE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::SMEM_BYTES);
+template <int KFIX>
+static int launch_gu(const DecodeArgs& a, int nclusters, int cs, cudaStream_t s) {
+    using C = StreamCfg<KFIX, 0>;
+    constexpr int smem = C::SMEM_BYTES + kTokPerEnt * 128 * 4;
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(gu_cluster_kernel<KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
-        attr_set = true;
+        attr_dev = dev;
     }
-    cudaError_t e = launch_k(stream_kernel<KFIX, PHASE>, dim3(grid), dim3(256), (size_t)C::SMEM_BYTES, s, a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nclusters * cs);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cs;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gu_cluster_kernel<KFIX>, a);
+    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    return 0;
+}
+
+template <int KFIX>
+static int launch_dn(const DecodeArgs& a, int grid, cudaStream_t s) {
+    using C = StreamCfg<KFIX, 1>;
+    constexpr int smem = C::SMEM_BYTES + 9 * kTokPerEnt * 128 * 4;
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(dn_item_kernel<KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+        attr_dev = dev;
+    }
+    cudaError_t e = launch_k(dn_item_kernel<KFIX>, dim3(grid), dim3(256), (size_t)smem, s, a);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     return 0;
 }
@@ -704,33 +1019,32 @@ static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int6
         int rc = victim_copy_launch(vict, host_base, slot_base, a.blob, a.E, hstride, ram_res, nvict, s);
         if (rc) return rc;
     }
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    // full machine for both phases (2 blocks of 8 warps per SM; 1 for the larger mixed-K ring); units are dealt
-    // block-major, so the per-SM share is equal even when there are fewer units than warps
-    long long max_gu = (long long)a.maxent * 2 * (I / 128) * (H / 128);
-    long long max_dn = (long long)a.maxent * (H / 128) * (I / 128);
-    int g1 = (int)std::min<long long>(std::max<long long>(max_gu, 1), (long long)nsm * (a.kinfo ? 1 : 2));
-    int g2 = (int)std::min<long long>(std::max<long long>(max_dn, 1), (long long)nsm * 2);
+    // gate-up: clusters of 4 CTAs (2 when H/128 is odd), one per (entry, 128-column block) up to a cap; down: one
+    // CTA per (entry, 128-column block of H) up to a cap; both loop over further items
+    const int nKB = H / 128;
+    const int cs = (nKB % 2 == 0) ? 4 : 2;
+    const long long gu_items = (long long)a.maxent * (I / 128);
+    const long long dn_items = (long long)a.maxent * (H / 128);
+    const int ncl = (int)std::min<long long>(std::max<long long>(gu_items, 1), 4096 / cs);
+    const int g2 = (int)std::min<long long>(std::max<long long>(dn_items, 1), 4096);
     int kf = a.kinfo ? 0 : a.K;
     int rc = 0;
     prof_record(1, s);
     switch (kf) {
-        case 0: rc = launch_stream<0, 0>(a, g1, s); break;
-        case 2: rc = launch_stream<2, 0>(a, g1, s); break;
-        case 3: rc = launch_stream<3, 0>(a, g1, s); break;
-        case 4: rc = launch_stream<4, 0>(a, g1, s); break;
-        case 5: rc = launch_stream<5, 0>(a, g1, s); break;
+        case 0: rc = launch_gu<0>(a, ncl, cs, s); break;
+        case 2: rc = launch_gu<2>(a, ncl, cs, s); break;
+        case 3: rc = launch_gu<3>(a, ncl, cs, s); break;
+        case 4: rc = launch_gu<4>(a, ncl, cs, s); break;
+        case 5: rc = launch_gu<5>(a, ncl, cs, s); break;
     }
     if (rc) return rc;
     prof_record(2, s);
     switch (kf) {
-        case 0: rc = launch_stream<0, 1>(a, g2, s); break;
-        case 2: rc = launch_stream<2, 1>(a, g2, s); break;
-        case 3: rc = launch_stream<3, 1>(a, g2, s); break;
-        case 4: rc = launch_stream<4, 1>(a, g2, s); break;
-        case 5: rc = launch_stream<5, 1>(a, g2, s); break;
+        case 0: rc = launch_dn<0>(a, g2, s); break;
+        case 2: rc = launch_dn<2>(a, g2, s); break;
+        case 3: rc = launch_dn<3>(a, g2, s); break;
+        case 4: rc = launch_dn<4>(a, g2, s); break;
+        case 5: rc = launch_dn<5>(a, g2, s); break;
     }
     if (rc) return rc;
     prof_record(3, s);

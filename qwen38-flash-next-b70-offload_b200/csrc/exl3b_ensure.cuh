@@ -109,6 +109,10 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     int mf = a.max_fill < E ? a.max_fill : E;
     int nm = S > 0 ? (total < mf ? total : mf) : 0;
     __syncthreads();   // slot_last stamps visible to the whole block
+    if (nm == 0) {     // every pick a hit (or masked): no slot scan
+        if (tid == 0) { a.fill_list[0] = 0; if (a.vict) a.vict[0] = 0; }
+        return;
+    }
     // 5. eligible slots (contiguous chunk per thread, ascending slot index overall)
     const int C = (S + kEnsureThreads - 1) / kEnsureThreads;
     const int s0 = tid * C, s1 = min(S, s0 + C);
