@@ -124,6 +124,15 @@ int exl3b_moe_decode_noalloc(const void* x, int64_t x_stride, int x_bf16, const 
                              int topk, const int64_t* ptrs, const int32_t* kinfo, int H, int I, int K, int E, void* out,
                              int64_t out_stride, int out_bf16, int flags, void* stream);
 
+/* Config-5 shared expert: replaces the model's shared_expert_gate (a bf16 Linear(H -> 1) + sigmoid around the
+ * shared expert, whose three linears go through exl3xpu_C.linear, experimental/n111-victim-ring/csrc/exl3_ops.sycl:
+ * 651-757).  Weight = 1 / (1 + expf(-dot(x[t], g))) with the router's dot-product arithmetic; writes the extended
+ * routing ids_out / w_out [T][topk + 1] = the routed picks, then (shared_id, weight).  The shared expert's blob (the
+ * routed layout, its own K per tensor) is entry shared_id of the pointer table given to the MoE layer, so it runs as
+ * one more pick per token and enters the combine after the routed picks. */
+int exl3b_shared_gate(const void* x_bf16, int64_t x_stride, const void* g_bf16, int T, int H, const int32_t* ids,
+                      const float* w, int topk, int shared_id, int32_t* ids_out, float* w_out, void* stream);
+
 /* Replaces moe_prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828 with GateUpDpasKernel :422-545, DownDpasKernel
  * :548-635 and CombineKernel :371-395), the path moe_forward takes for M >= prefill_min_m (:1263-1314): the routed-MoE
  * layer for many tokens as grouped tensor-core GEMMs (tcgen05, fp16 operands, fp32 accumulate in TMEM).  Arguments as

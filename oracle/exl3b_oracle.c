@@ -480,6 +480,17 @@ EXPORT void ora_dense_glu(const uint16_t* x, int x_is_bf16, const uint8_t* blob,
     free(wg); free(wu); free(wd); free(abuf);
 }
 
+/*
+ * Shared-expert gate (config 5; the model's shared_expert_gate, a bf16 Linear(H -> 1) followed by a sigmoid):
+ * s = dot(x, g) with the router's arithmetic (ora_router_dot), weight = 1 / (1 + expf(-s)).  The shared expert
+ * then enters the combine as one more pick per token, after the routed picks.
+ */
+EXPORT float ora_router_dot(const uint16_t* x, const uint16_t* wr, int H);
+EXPORT float ora_shared_gate(const uint16_t* x, const uint16_t* g, int H) {
+    const float s = ora_router_dot(x, g, H);
+    return 1.0f / (1.0f + expf(-s));
+}
+
 /* ------------------------------------------------------------------------------------------------
  * Router (SGLang TopK semantics consumed at plugin/sglang_plugin.tier.py:534-535, 560; SGLang itself
  * is not vendored, so this build defines the arithmetic exactly and the CUDA kernel follows it):

@@ -64,6 +64,7 @@ def lib():
             "ora_dense_glu": (None, [u16p, ci, vp, ci, ci, ci, ci, ci, f32p]),
             "ora_expert_picks": (None, [u16p, ctypes.c_int64, ci, i32p, f32p, ci, vp, ci, ci, ci, ci, ci, ci, f32p]),
             "ora_router_dot": (ctypes.c_float, [u16p, u16p, ci]),
+            "ora_shared_gate": (ctypes.c_float, [u16p, u16p, ci]),
             "ora_router": (None, [u16p, u16p, vp, ci, ci, ci, ci, i32p, f32p, vp]),
             "ora_align": (None, [i32p, f32p, ci, ci, ci, ci, i32p, i32p, i32p, i32p, i32p, i32p, f32p, i32p, vp, vp]),
             "ora_ensure": (ci, [i32p, f32p, ci, ci, ci, ci, i64p, i32p, i32p, i32p, i32p, i64p, i64, i64, i64, i64p,
@@ -205,6 +206,14 @@ def moe_layer_fast(x_bits: np.ndarray, ids: np.ndarray, w: np.ndarray, blobs: li
         return acc
     u = acc.view(np.uint32)
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16) if x_is_bf16 else acc.astype(np.float16).view(np.uint16)
+
+
+def shared_gate(x_bits: np.ndarray, g_bits: np.ndarray) -> np.ndarray:
+    """Shared-expert gate weights sigmoid(x . g) fp32 [M] (router dot-product arithmetic) for x bf16 bits [M, H]."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    g_bits = np.ascontiguousarray(g_bits, dtype=np.uint16)
+    M, H = x_bits.shape
+    return np.array([lib().ora_shared_gate(np.ascontiguousarray(x_bits[m]), g_bits, H) for m in range(M)], dtype=np.float32)
 
 
 def dense_glu(x_bits: np.ndarray, blob: np.ndarray, H: int, I: int, Kg: int, Ku: int, Kd: int) -> np.ndarray:

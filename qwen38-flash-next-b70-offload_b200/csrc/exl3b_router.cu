@@ -122,9 +122,55 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
     if (threadIdx.x == 0) *counter = 0;
 }
 
+// Shared-expert gate (config 5): one warp per token; s = dot(x[t], g) with the router's arithmetic (lane c sums
+// chunk c in ascending k with fp32 fma, xor butterfly 16..1), weight = 1 / (1 + expf(-s)).  Writes the extended
+// routing [T][topk + 1]: the token's routed picks, then (shared_id, weight).
+__global__ void __launch_bounds__(256) shared_gate_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
+                                                          const __nv_bfloat16* __restrict__ g, int T, int H,
+                                                          const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                          int topk, int shared_id, int32_t* __restrict__ ids_out,
+                                                          float* __restrict__ w_out) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const int cl = H / 32;
+    const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + (long long)t * xs + lane * cl;
+    const uint16_t* gr = reinterpret_cast<const uint16_t*>(g) + lane * cl;
+    float acc = 0.0f;
+    for (int k = 0; k < cl; ++k)
+        acc = __fmaf_rn(__uint_as_float((uint32_t)xr[k] << 16), __uint_as_float((uint32_t)gr[k] << 16), acc);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    const int k1 = topk + 1;
+    for (int k = lane; k < topk; k += 32) {
+        ids_out[(long long)t * k1 + k] = ids[(long long)t * topk + k];
+        w_out[(long long)t * k1 + k] = w[(long long)t * topk + k];
+    }
+    if (lane == 0) {
+        ids_out[(long long)t * k1 + topk] = shared_id;
+        w_out[(long long)t * k1 + topk] = 1.0f / (1.0f + expf(-acc));
+    }
+}
+
 }  // namespace exl3b
 
 using namespace exl3b;
+
+extern "C" EXL3B_API int exl3b_shared_gate(const void* x_bf16, int64_t x_stride, const void* g_bf16, int T, int H,
+                                           const int32_t* ids, const float* w, int topk, int shared_id,
+                                           int32_t* ids_out, float* w_out, void* stream) {
+    EXL3B_CHECK(x_bf16 && g_bf16 && ids && w && ids_out && w_out, "exl3b_shared_gate: null pointer");
+    EXL3B_CHECK(H % 32 == 0 && H > 0 && topk >= 1 && shared_id >= 0, "exl3b_shared_gate: H % 32 == 0, topk >= 1");
+    EXL3B_CHECK(x_stride >= H, "exl3b_shared_gate: row stride must be >= H");
+    if (T <= 0) return 0;
+    cudaError_t e = launch_k(shared_gate_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, (cudaStream_t)stream,
+                             (const __nv_bfloat16*)x_bf16, (long long)x_stride, (const __nv_bfloat16*)g_bf16, T, H, ids, w,
+                             topk, shared_id, ids_out, w_out);
+    if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+    return 0;
+}
 
 extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias,
                                            int T, int H, int E, int topk, int32_t* ids, float* w, float* logits,

@@ -187,6 +187,31 @@ def _moe_forward_mixed_impl(x, topk_ids, topk_w, ptrs, kinfo, I, n_experts):
     return moe_decode(x, topk_ids, topk_w, ptrs, I, 0, n_experts, kinfo=kinfo)
 
 
+def shared_gate(x: torch.Tensor, gate_w: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, shared_id: int):
+    """Config-5 shared-expert gate: returns the extended routing (ids [T, topk + 1], w [T, topk + 1]) with the shared
+    expert (id shared_id, weight sigmoid(x . gate_w)) after the routed picks."""
+    if x.dtype != torch.bfloat16 or gate_w.dtype != torch.bfloat16 or x.stride(1) != 1 or not gate_w.is_contiguous():
+        raise RuntimeError("exl3b200 shared_gate: bf16 x with unit-stride rows and contiguous bf16 gate_w")
+    _check_route(ids, w)
+    T, H = x.shape
+    topk = ids.shape[1]
+    ids_out = torch.empty((T, topk + 1), dtype=torch.int32, device=x.device)
+    w_out = torch.empty((T, topk + 1), dtype=torch.float32, device=x.device)
+    check(_lib.lib().exl3b_shared_gate(x.data_ptr(), x.stride(0), gate_w.data_ptr(), T, H, ids.data_ptr(), w.data_ptr(),
+                                       topk, int(shared_id), ids_out.data_ptr(), w_out.data_ptr(), stream(x.device)),
+          "shared_gate")
+    return ids_out, w_out
+
+
+def _moe_forward_shared_impl(x, topk_ids, topk_w, ptrs, kinfo, gate_w, I, n_experts):
+    """Routed experts plus the always-on shared expert (config 5): ptrs / kinfo hold n_experts + 1 entries, the shared
+    expert last; it runs as one more pick per token with weight sigmoid(x . gate_w), combined after the routed picks."""
+    if ptrs.numel() != n_experts + 1 or kinfo.numel() != n_experts + 1:
+        raise RuntimeError("exl3b200 moe_forward_shared: ptrs and kinfo need n_experts + 1 entries (shared last)")
+    ids_x, w_x = shared_gate(x, gate_w, topk_ids, topk_w, n_experts)
+    return _moe_forward_mixed_impl(x, ids_x, w_x, ptrs, kinfo, I, n_experts + 1)
+
+
 def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
                              slot_base, fill_all, fill_list, max_fill, I, K, n_experts, pend, done_seq, out=None):
     if ptrs_all.dtype != torch.int64 or fill_all.dtype != torch.int64 or slot_of.dtype != torch.int32:
@@ -378,10 +403,14 @@ def register() -> None:
     lib.impl("moe_align", _moe_align_impl, "CUDA")
     lib.impl("router_topk", lambda x, wr, bias, topk: router_topk(x, wr, bias, topk), "CUDA")
     lib.impl("moe_forward_mixed", _moe_forward_mixed_impl, "CUDA")
+    lib.define("moe_forward_shared(Tensor x, Tensor topk_ids, Tensor topk_w, Tensor ptrs, Tensor kinfo, Tensor gate_w, "
+               "int I, int n_experts) -> Tensor")
+    lib.impl("moe_forward_shared", _moe_forward_shared_impl, "CUDA")
 
     torch.library.register_fake(f"{NS}::moe_forward", lambda x, *a: torch.empty_like(x), lib=lib)
     torch.library.register_fake(f"{NS}::moe_forward_cached", lambda x, *a: torch.empty_like(x), lib=lib)
     torch.library.register_fake(f"{NS}::moe_forward_mixed", lambda x, *a: torch.empty_like(x), lib=lib)
+    torch.library.register_fake(f"{NS}::moe_forward_shared", lambda x, *a: torch.empty_like(x), lib=lib)
     globals()["_torch_lib"] = lib
     _registered = True
 
@@ -392,7 +421,8 @@ class _Ops:
     def __getattr__(self, name):
         register()
         if hasattr(torch.ops.exl3b200_moe, name) and name in ("moe_forward", "moe_forward_cached", "moe_prefetch",
-                                                               "moe_align", "router_topk", "moe_forward_mixed"):
+                                                               "moe_align", "router_topk", "moe_forward_mixed",
+                                                               "moe_forward_shared"):
             return getattr(torch.ops.exl3b200_moe, name)
         fn = {"host_alloc": host_alloc, "usm_kind": usm_kind, "memcpy_async": memcpy_async,
               "blob_bytes": blob_bytes, "moe_set_splits": moe_set_splits, "moe_set_mr": moe_set_mr,
