@@ -133,6 +133,22 @@ int exl3b_moe_decode_noalloc(const void* x, int64_t x_stride, int x_bf16, const 
 int exl3b_shared_gate(const void* x_bf16, int64_t x_stride, const void* g_bf16, int T, int H, const int32_t* ids,
                       const float* w, int topk, int shared_id, int32_t* ids_out, float* w_out, void* stream);
 
+/* ---- expert-parallel prefill (configs[3]; the reference's moe_prefill, exl3_moe.a8.sycl:792-828, runs on one GPU:
+ * this is its extension over G GPUs of one node, around NCCL all-to-all exchanges done by the host).
+ * Experts are sharded contiguously, rank d owning ids [d E/G, (d+1) E/G).  exl3b_ep_plan: for the T local tokens'
+ * routing ids / w [T][topk] (id -1 = no pick), bits [T] scratch, counts [G] / offs [G+1] (int64) rows per
+ * destination and their offsets, pos [T][G] = send row of (t, d) or -1 (destination-major, ascending t), and per
+ * send row (at most T G): send_src (source token), send_ids / send_w [topk] (the destination's local expert ids,
+ * -1 for picks owned by other ranks).  exl3b_ep_pack: send_x[row] = x[send_src[row]] (16-bit rows).
+ * exl3b_ep_combine: out[t] = sum over d ascending of part[pos[t][d]] (fp32 partial sums returned by the
+ * destinations), out_kind 0 fp16, 1 bf16, 2 fp32. */
+int exl3b_ep_plan(const int32_t* ids, const float* w, int T, int topk, int E, int G, uint32_t* bits, int64_t* counts,
+                  int64_t* offs, int32_t* pos, int32_t* send_src, int32_t* send_ids, float* send_w, void* stream);
+int exl3b_ep_pack(const void* x, int64_t x_stride, int H, const int32_t* send_src, int n_rows, void* send_x,
+                  void* stream);
+int exl3b_ep_combine(const float* part, const int32_t* pos, int T, int G, int H, void* out, int64_t out_stride,
+                     int out_kind, void* stream);
+
 /* Replaces moe_prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828 with GateUpDpasKernel :422-545, DownDpasKernel
  * :548-635 and CombineKernel :371-395), the path moe_forward takes for M >= prefill_min_m (:1263-1314): the routed-MoE
  * layer for many tokens as grouped tensor-core GEMMs (tcgen05, fp16 operands, fp32 accumulate in TMEM).  Arguments as

@@ -560,7 +560,8 @@ EXPORT void ora_align(const int32_t* ids, const float* w, int npairs, int topk, 
     int* cnt = (int*)calloc((size_t)E, sizeof(int));
     int* start = (int*)calloc((size_t)E, sizeof(int));
     int* fill = (int*)calloc((size_t)E, sizeof(int));
-    for (int i = 0; i < npairs; ++i) cnt[ids[i]]++;
+    /* id -1 is "no pick" (an expert-parallel rank's picks owned by other ranks): not placed, pair_of = -1 */
+    for (int i = 0; i < npairs; ++i) if (ids[i] >= 0) cnt[ids[i]]++;
     int st = 0, pst = 0, na = 0;
     for (int e = 0; e < E; ++e) {
         start[e] = st;
@@ -577,6 +578,7 @@ EXPORT void ora_align(const int32_t* ids, const float* w, int npairs, int topk, 
     if (n_blk) *n_blk = pst / pad;
     for (int i = 0; i < npairs; ++i) {
         int e = ids[i];
+        if (e < 0) { pair_of[i] = -1; continue; }
         int pos = start[e] + fill[e]++;
         pair_tok[pos] = i / topk;
         pair_w[pos] = w[i];

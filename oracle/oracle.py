@@ -181,7 +181,7 @@ def moe_layer_fast(x_bits: np.ndarray, ids: np.ndarray, w: np.ndarray, blobs: li
     flat_w = sw.ravel()
     y = np.zeros((M * topk, H), dtype=np.float32)
     L = lib()
-    experts = np.unique(flat_e)
+    experts = np.unique(flat_e[flat_e >= 0])   # id -1: no pick (its output row stays zero)
 
     def run(e):
         sel = np.nonzero(flat_e == e)[0]

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(kAlignBlock) align_hist_kernel(const int32_t* 
     if (i < P) {
         int e = ids[i];
         if (e >= 0 && e < E) atomicAdd(&h[e], 1);
-        else set_error(kErrBounds);
+        else if (e != -1) set_error(kErrBounds);   // -1: no pick (expert-parallel ranks), skipped
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) bc[(size_t)blockIdx.x * E + e] = h[e];
@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kAlignBlock) align_place_kernel(const int32_t*
     unsigned peers = __match_any_sync(0xffffffffu, ok ? e : -1);
     int rank = __popc(peers & ((1u << lane) - 1u));
     int leader_last = 31 - __clz(peers);   // highest lane of the group updates the running count
+    if (i < P && !ok) o.pair_of[i] = -1;   // not placed: the combine skips it
     for (int s = 0; s < 32; ++s) {
         if (wid == s && ok) {
             int pos = start[e] + bc[(size_t)blockIdx.x * E + e] + run[e] + rank;

@@ -76,7 +76,7 @@ __device__ __forceinline__ void route_prep_block(const DecodeArgs& a) {
             int e = a.ids[i];
             bool ok = e >= 0 && e < a.E;
             bool act = ok && !(a.skip_zero && a.w[i] == 0.0f);
-            if (!ok) set_error(kErrBounds);
+            if (!ok && e != -1) set_error(kErrBounds);   // -1: no pick (expert-parallel ranks)
             a.pick_act[i] = act ? 1 : 0;
             s_ids[i - c0] = act ? e : -1;
             if (act) atomicAdd(&cnt[e], 1);
@@ -157,7 +157,7 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
     const int kpack = a.K | (a.K << 4) | (a.K << 8);
     int id[J];
     float wv[J];
-    bool val[J];
+    bool val[J], none[J] = {false, false, false, false};
     bool bad = false;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
@@ -165,6 +165,7 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
         val[j] = i < np;
         id[j] = val[j] ? a.ids[i] : 0;
         wv[j] = val[j] ? a.w[i] : 0.0f;
+        if (val[j] && id[j] == -1 && !cached) { val[j] = false; none[j] = true; }   // no pick
         bad |= val[j] && (id[j] < 0 || id[j] >= E);
     }
     if (__any_sync(FULL, bad)) return false;
@@ -262,7 +263,7 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const int i = lane + 32 * j;
-        if (val[j]) a.pick_act[i] = act[j] ? 1 : 0;
+        if (val[j] || none[j]) a.pick_act[i] = act[j] ? 1 : 0;
         if (!act[j]) continue;
         const int e8 = en[j] * kTokPerEnt;
         if (sl[j] == 0) {

@@ -535,7 +535,8 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillArgs p) {
     const int t = (int)(gid / nc), c8 = (int)(gid % nc) * 8;
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < p.topk; ++k) {
-        int pr = p.pair_of[t * p.topk + k];
+        const int pr = p.pair_of[t * p.topk + k];
+        if (pr < 0) continue;   // no pick (id -1)
         uint4 q = *reinterpret_cast<const uint4*>(p.y + (size_t)pr * p.H + c8);
         const __half2* h = reinterpret_cast<const __half2*>(&q);
 #pragma unroll

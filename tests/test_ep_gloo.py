@@ -1,0 +1,91 @@
+"""CPU, world_size 2 (gloo): the expert-parallel prefill exchange (exl3b200.ep.EPPrefill) with host stand-ins for
+the device steps.  Every rank's output equals the one-device prefill of its tokens (oracle, same picks) within the
+layer tolerance; a rank with no tokens and a rank whose tokens all stay local are covered."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, case, q):
+    import sys
+    sys.path[:0] = [os.path.join(ROOT, "qwen38-flash-next-b70-offload_b200"), os.path.join(ROOT, "oracle"),
+                    os.path.join(ROOT, "tests")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import oracle as O
+        from ep_host import HostEPKernels
+        from exl3b200 import synth
+        from exl3b200.ep import EPPrefill
+        from helpers import assert_close_layer
+        E, H, I, K, topk = 8, 256, 128, 3, 3
+        per = E // world
+        blobs = [synth.make_blob(11, e, H, I, K).numpy() for e in range(E)]
+        T = case["T"][rank]
+        g = torch.Generator().manual_seed(100 + rank)
+        if case.get("local_only") and rank == 0:
+            ids = torch.stack([torch.randperm(per, generator=g)[:topk] for _ in range(T)]).to(torch.int32)
+        else:
+            ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).to(torch.int32) if T else \
+                torch.zeros((0, topk), dtype=torch.int32)
+        w = torch.rand(T, topk, generator=g)
+        w = (w / w.sum(1, keepdim=True)).float() if T else torch.zeros((0, topk))
+        x = synth.activations(T, H, 200 + rank) if T else torch.zeros((0, H), dtype=torch.bfloat16)
+        k = HostEPKernels(blobs[rank * per:(rank + 1) * per], H, I, K)
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, torch.zeros(per, dtype=torch.int64), kernels=k)
+        out = ep.forward(x, ids, w)
+        if T:
+            xb = x.view(torch.int16).numpy().view(np.uint16)
+            ref = O.moe_layer_fast(xb, ids.numpy(), w.numpy(), blobs, H, I, K, y_half=True, threads=2)
+            assert_close_layer(out.view(torch.int16).numpy().view(np.uint16), ref)
+        q.put((rank, "ok", ep.last))
+    except Exception as e:   # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}", None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(case):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, status, _ in res:
+        assert status == "ok", f"rank {rank}: {status}"
+    return {r: last for r, _, last in res}
+
+
+def test_ep_exchange_two_ranks():
+    last = _run({"T": [7, 5]})
+    assert last[0]["send_rows"] > 0 and last[1]["recv_rows"] > 0
+
+
+def test_ep_rank_without_tokens():
+    _run({"T": [6, 0]})
+
+
+def test_ep_tokens_all_local():
+    last = _run({"T": [5, 4], "local_only": True})
+    assert last[0]["send_counts"][1] == 0
