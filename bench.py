@@ -31,6 +31,9 @@ SEED = 0
 GU_BYTES = (H // 16) * (2 * I // 16) * 8 * K * 4     # gate|up codes per expert: 1,179,648 B
 BLOB = 1786368
 PF_T = 8192          # configs[2] prefill chunk
+# DRAM bytes (read + write) of one decode gate-up launch at batch 1, from one ncu capture of gu_cluster_kernel<3> on
+# the same per-layer work (4-layer stack): dram__bytes_read.sum + dram__bytes_write.sum
+GU_TRAFFIC_BS1 = 12013312
 PF_KEY0 = 1 << 20    # blob keys of the prefill layer (distinct from the decode stack's)
 # router weight std: x . Wr then has the std of a standard Gumbel variable (pi / sqrt(6) = 1.28), so -1.1 ln(rank) +
 # router noise makes each layer's top-10 a Zipf(1.1)-like Plackett-Luce sample and picks miss the 8,000-slot cache
@@ -319,6 +322,68 @@ def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T):
             "config": "configs[2]: 1 layer, 8192 tokens, 512 experts resident, top-10, K=3, logits N(0,1) + bias N(0,1.5)"}
 
 
+def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, warmup=3):
+    """expert-parallel prefill of the 48-layer stack, T_total tokens per batch split evenly over the ranks
+    (strong scaling), the 512 experts sharded contiguously (rank d holds experts [d 512/N, (d+1) 512/N)); NCCL
+    all-to-all dispatch and combine around each rank's grouped GEMMs (exl3b200.ep.EPPrefill).  Every layer has its
+    own router, bias and inputs; the layers share one synthetic set of 512 experts (915 MB per layer, far above the
+    126 MB L2, so sharing the bytes does not change what a layer costs).  Routing is computed before timing.  With
+    one GPU the same stack runs through the single-GPU prefill.  Device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from exl3b200 import synth
+    from exl3b200 import ops as X
+    per = E // world
+    arena = torch.empty((per, BLOB), dtype=torch.uint8, device=dev)
+    synth.fill_blobs(arena, SEED, [PF_KEY0 + rank * per + e for e in range(per)], H, I, K)
+    ptrs_local = (arena.data_ptr() + torch.arange(per, dtype=torch.int64) * BLOB).to(dev)
+    T = T_total // world
+    xs, routes = [], []
+    for li in range(layers):
+        x = synth.activations(T, H, 5000 + 97 * li + rank).to(dev)
+        wr = synth.router_weight(E, H, 1.0 / H ** 0.5, SEED + 3000 + li).to(dev)
+        bias = synth.normal_bias(E, 1.5, SEED + li).to(dev)
+        ids, w = X.router_topk(x, wr, bias, TOPK)
+        xs.append(x)
+        routes.append((ids, w))
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        from exl3b200.ep import EPPrefill
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs_local)
+        run = lambda li: ep.forward(xs[li], *routes[li])
+    else:
+        run = lambda li: X.moe_prefill(xs[li], routes[li][0], routes[li][1], ptrs_local, I, K, E)
+    for _ in range(warmup):
+        for li in range(layers):
+            run(li)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        for li in range(layers):
+            run(li)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    flops = 2.0 * T_total * TOPK * 3 * H * I * layers
+    _, tc, _ = peaks()
+    out = {"tokens_per_batch": T_total, "layers": layers, "value": round(T_total * 1000.0 / ms, 1),
+           "unit": "tok/s (48-layer stack)", "ms_per_step": round(ms, 3), "n_gpus": world, "scaling": "strong",
+           "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world, 1),
+           "frac_of_peak_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world / tc, 4),
+           "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if world > 1 else "one GPU",
+           "config": "configs[3]: 48 layers, logits N(0,1) + bias N(0,1.5), top-10, K=3, experts sharded by id"}
+    del arena, xs, routes
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -335,6 +400,14 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     X.register()
     T = args.batch
+    if args.only == "prefill":
+        pf = measure_prefill(dev, local, T=args.pf_tokens)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "prefill": pf}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     st, wr, bias, xs, ring = build_stack(dev, T)
     if world > 1:
         dist.barrier()
@@ -353,11 +426,13 @@ def run_ours(args):
                             "down_combine": round(1e3 * sum(d4["dn_ms"]) / len(d4["dn_ms"]), 2)}}
         del xs4
     X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32))
-    pf = None
+    pf = pf_ep = None
     if not args.no_prefill:
         del st
         torch.cuda.empty_cache()
-        pf = measure_prefill(dev, local)
+        if world == 1:
+            pf = measure_prefill(dev, local, T=args.pf_tokens)
+        pf_ep = measure_prefill_ep(dev, local, world, rank, args.ep_tokens)
     hbm, tc, src = peaks()
     distinct = d["distinct"]
     avg_distinct = sum(distinct) / L
@@ -383,7 +458,8 @@ def run_ours(args):
         "e2e": {"value": round(world * T * 1000.0 / ms_e2e, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": d["h2d"], "d2h_bytes_per_step": d["d2h"]},
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                     "traffic": None, "kernel": "gu_cluster_kernel<3> (decode gate-up)", "peak_source": src,
+                     "traffic": GU_TRAFFIC_BS1 if T == 1 else None, "kernel": "gu_cluster_kernel<3> (decode gate-up)",
+                     "peak_source": src,
                      "algorithmic_bytes_per_launch": int(gu_bytes), "avg_launch_us": round(gu_s * 1e6, 2)},
         "layer_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
                       "frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
@@ -397,6 +473,8 @@ def run_ours(args):
         line["bs4"] = bs4
     if pf is not None:
         line["prefill"] = pf
+    if pf_ep is not None:
+        line["prefill_ep"] = pf_ep
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(d["id_buf"], d["w_buf"], T, seconds=args.cpu_seconds)
     if world > 1:
@@ -507,10 +585,20 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-bs4", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--ep-tokens", type=int, default=8192, help="configs[3] tokens per batch (8192 or 32768)")
+    ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
+                    help="decode: skip both prefill measurements; prefill: only the configs[2] layer (small profiling runs)")
+    ap.add_argument("--layers", type=int, default=48, help="decode stack depth (48; fewer only for small profiling runs)")
+    ap.add_argument("--slots", type=int, default=8000, help="device cache slots (8000; fewer for small profiling runs)")
+    ap.add_argument("--pf-tokens", type=int, default=8192, help="configs[2] prefill tokens")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    global L, S
+    L, S = args.layers, args.slots
+    if args.only == "decode":
+        args.no_prefill = True
     if args.impl == "reference":
         run_reference(args)
     else:
