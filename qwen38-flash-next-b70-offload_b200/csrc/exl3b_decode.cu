@@ -47,6 +47,27 @@ struct DecodeArgs {
     int* cnt_gu; int* cnt_d; int* cnt_c; int* blocks_done;
     __half* abuf; float* part_gu; float* part_d; float* y;
     int maxent;
+    // small batches (M <= kTokPerEnt, M topk <= kSmallPicks): the gate-up and down kernels group the picks themselves
+    // from ids / w and the layer's tier state (t_*: null without a cache or tier); the tier mask's in-place rewrite
+    // of ids / w is then done by the last down block
+    int small;
+    const int32_t* t_slot_of; const uint8_t* t_ram_res; const int32_t* t_safe;
+};
+
+constexpr int kSmallPicks = 32;   // small-batch mode: up to 32 picks (3 tokens at top-10)
+
+// Grouping of a small batch in shared memory (the entry tables of route_prep_block, plus per-pick flags).
+struct SmallTab {
+    long long blob[kSmallPicks];
+    int kv[kSmallPicks];
+    float w[kSmallPicks][kTokPerEnt];
+    unsigned char ntok[kSmallPicks];
+    unsigned char tok[kSmallPicks][kTokPerEnt];
+    unsigned char pick[kSmallPicks][kTokPerEnt];
+    unsigned char act[kSmallPicks];      // pick active (weight != 0 when skipping zero weights)
+    unsigned char masked[kSmallPicks];   // tier-masked: becomes (safe, 0)
+    unsigned char tok_cnt[kTokPerEnt];
+    int n, safe;
 };
 
 // ------------------------------------------------------------------------------------------------ prep
@@ -205,8 +226,10 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
             if (masked[j]) {
                 const int i = lane + 32 * j;
                 ea.ring[1 + ((base + __popc(bm & lt)) % ea.ring_cap)] = L * E + id[j];
-                ea.ids[i] = safe;
-                ea.w[i] = 0.0f;
+                if (!ea.defer_mask) {   // deferred: the last down block rewrites ids / w
+                    ea.ids[i] = safe;
+                    ea.w[i] = 0.0f;
+                }
                 id[j] = safe; wv[j] = 0.0f; so[j] = so_safe; pt[j] = pt_safe; kv[j] = kv_safe;
             }
             base += __popc(bm);
@@ -293,6 +316,98 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
         }
     }
     return true;
+}
+
+// One warp groups a small batch into tb (the caller synchronises the block afterwards): the same entries, pick
+// order and token counts as prep's grouping after the tier mask, computed from the call's ids / w (read from L2:
+// they were written by kernels before this one) and the read-only tier state.  Concurrent cache-state writes by the
+// prep kernel do not change the result: a miss keeps reading its host copy until the commit, and the mask of a
+// picked key does not depend on slot assignment.
+__device__ __forceinline__ void group_small(const DecodeArgs& a, SmallTab& tb) {
+    constexpr int J = kSmallPicks / 32;
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int np = a.M * a.topk, E = a.E;
+    const int kpack = a.K | (a.K << 4) | (a.K << 8);
+    const bool tier = a.t_ram_res != nullptr && a.t_slot_of != nullptr && a.t_safe != nullptr;
+    const int safe = tier ? __ldcg(a.t_safe) : 0;
+    int id[J], kv[J];
+    float wv[J];
+    long long pt[J];
+    bool act[J], msk[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        const bool val = i < np;
+        int e = val ? __ldcg(a.ids + i) : -1;
+        float ww = val ? __ldcg(a.w + i) : 0.0f;
+        const bool inr = e >= 0 && e < E;
+        msk[j] = false;
+        if (inr && tier && __ldcg(a.t_slot_of + e) < 0 && __ldcg(a.t_ram_res + e) == 0) {
+            msk[j] = true;
+            e = safe;
+            ww = 0.0f;
+        }
+        id[j] = e;
+        wv[j] = ww;
+        act[j] = inr && !(a.skip_zero && ww == 0.0f);
+        pt[j] = act[j] ? (long long)__ldcg(a.ptrs + e) : 0;
+        kv[j] = (act[j] && a.kinfo) ? __ldcg(a.kinfo + e) : kpack;
+    }
+    int sl[J], cnt[J], en[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) { sl[j] = 0; cnt[j] = 0; en[j] = 0; }
+#pragma unroll
+    for (int qj = 0; qj < J; ++qj) {
+        if (qj * 32 >= np) break;
+        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
+            const int eq = __shfl_sync(FULL, id[qj], ql);
+            const int aq = __shfl_sync(FULL, (int)act[qj], ql);
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                if (act[j] && aq && eq == id[j]) {
+                    ++cnt[j];
+                    if (qj * 32 + ql < lane + 32 * j) ++sl[j];
+                }
+        }
+    }
+    int ndist = 0;
+#pragma unroll
+    for (int qj = 0; qj < J; ++qj) {
+        if (qj * 32 >= np) break;
+        const bool first_q = act[qj] && sl[qj] == 0;
+        ndist += __popc(__ballot_sync(FULL, first_q));
+        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
+            const int eq = __shfl_sync(FULL, id[qj], ql);
+            const int fq = __shfl_sync(FULL, (int)first_q, ql);
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                if (fq && eq < id[j]) ++en[j];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        if (i < kSmallPicks) { tb.act[i] = act[j] ? 1 : 0; tb.masked[i] = msk[j] ? 1 : 0; }
+        if (!act[j]) continue;
+        if (sl[j] == 0) {
+            tb.blob[en[j]] = pt[j];
+            tb.kv[en[j]] = kv[j];
+            tb.ntok[en[j]] = (unsigned char)cnt[j];
+            for (int q = cnt[j]; q < kTokPerEnt; ++q) { tb.tok[en[j]][q] = 0; tb.pick[en[j]][q] = 0; tb.w[en[j]][q] = 0.0f; }
+        }
+        tb.tok[en[j]][sl[j]] = (unsigned char)(i / a.topk);
+        tb.pick[en[j]][sl[j]] = (unsigned char)i;
+        tb.w[en[j]][sl[j]] = wv[j];
+    }
+    for (int m = 0; m < a.M; ++m) {
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < J; ++j) c += (act[j] && (lane + 32 * j) / a.topk == m) ? 1 : 0;
+        c = __reduce_add_sync(FULL, (unsigned)c);
+        if (lane == 0) tb.tok_cnt[m] = (unsigned char)c;
+    }
+    if (lane == 0) { tb.n = ndist; tb.safe = safe; }
 }
 
 // Cached calls run the device cache step first (in place on ids / w), then the grouping.  Small batches try the
@@ -392,7 +507,7 @@ struct UMeta {
 };
 
 template <int PHASE>
-__device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_units) {
+__device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_units, const SmallTab* tb) {
     UMeta m;
     const int lane = threadIdx.x & 31;
     m.valid = u < n_units;
@@ -411,12 +526,20 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
         m.f1 = u % nKBd; int r = u / nKBd;
         m.f0 = r % nbH; m.ent = r / nbH; m.f2 = 0;
     }
-    m.blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + m.ent));
-    m.ntok = __ldcg(a.ent_n + m.ent);
-    m.kv = __ldcg(a.ent_k + m.ent);
+    if (tb) {
+        m.blob = reinterpret_cast<const uint8_t*>(tb->blob[m.ent]);
+        m.ntok = tb->ntok[m.ent];
+        m.kv = tb->kv[m.ent];
+        m.tok = lane < kTokPerEnt ? tb->tok[m.ent][lane] : 0;
+        m.pick = lane < kTokPerEnt ? tb->pick[m.ent][lane] : 0;
+    } else {
+        m.blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + m.ent));
+        m.ntok = __ldcg(a.ent_n + m.ent);
+        m.kv = __ldcg(a.ent_k + m.ent);
+        m.tok = lane < kTokPerEnt ? __ldcg(a.ent_tok + m.ent * kTokPerEnt + lane) : 0;
+        m.pick = lane < kTokPerEnt ? __ldcg(a.ent_pick + m.ent * kTokPerEnt + lane) : 0;
+    }
     m.K = PHASE == 0 ? (m.f0 ? (m.kv >> 4) & 15 : m.kv & 15) : (m.kv >> 8) & 15;
-    m.tok = lane < kTokPerEnt ? __ldcg(a.ent_tok + m.ent * kTokPerEnt + lane) : 0;
-    m.pick = lane < kTokPerEnt ? __ldcg(a.ent_pick + m.ent * kTokPerEnt + lane) : 0;
     const Geom gm{a.H, a.I, m.kv & 15, (m.kv >> 4) & 15, (m.kv >> 8) & 15};
     const uint32_t* words = reinterpret_cast<const uint32_t*>(m.blob);
     if (PHASE == 0) {
@@ -525,16 +648,16 @@ struct GuEpi {
     uint2 svg, svu, sud;
     int pick;
 };
-__device__ __forceinline__ GuEpi gu_epi_load(const DecodeArgs& a, int ent, int nb, int t) {
+__device__ __forceinline__ GuEpi gu_epi_load(const DecodeArgs& a, int ent, int nb, int t, const SmallTab* tb) {
     const int lane = threadIdx.x & 31;
-    const int kv = __ldcg(a.ent_k + ent);
-    const uint8_t* blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + ent));
+    const int kv = tb ? tb->kv[ent] : __ldcg(a.ent_k + ent);
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(tb ? tb->blob[ent] : __ldcg(a.ent_blob + ent));
     const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
     GuEpi q;
     q.svg = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_g()) + nb * 128 + 4 * lane));
     q.svu = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_u()) + nb * 128 + 4 * lane));
     q.sud = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_suh_d()) + nb * 128 + 4 * lane));
-    q.pick = __ldcg(a.ent_pick + ent * kTokPerEnt + t);
+    q.pick = tb ? tb->pick[ent][t] : __ldcg(a.ent_pick + ent * kTokPerEnt + t);
     return q;
 }
 
@@ -568,15 +691,16 @@ __device__ __forceinline__ void gu_token_epilogue(const DecodeArgs& a, const GuE
 
 // Down (:355-364): y = FWHT(v) (r w) svh_d (fp32); then the combine (:387-394) of the token's 128-block by the last
 // of its active picks to finish: out[m] = sum_k y[m,k] in fixed k order.
-__device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, int nbh, int t, const float v_in[4]) {
+__device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, int nbh, int t, const float v_in[4],
+                                                  const SmallTab* tb) {
     const int lane = threadIdx.x & 31;
     const int nbH = a.H / 128;
-    const int kv = __ldcg(a.ent_k + ent);
-    const uint8_t* blob = reinterpret_cast<const uint8_t*>(__ldcg(a.ent_blob + ent));
+    const int kv = tb ? tb->kv[ent] : __ldcg(a.ent_k + ent);
+    const uint8_t* blob = reinterpret_cast<const uint8_t*>(tb ? tb->blob[ent] : __ldcg(a.ent_blob + ent));
     const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
     const __half* svd = reinterpret_cast<const __half*>(blob + gm.off_svh_d()) + nbh * 128 + 4 * lane;
-    const int pick = __ldcg(a.ent_pick + ent * kTokPerEnt + t);
-    const float wt = __ldcg(a.ent_w + ent * kTokPerEnt + t);
+    const int pick = tb ? tb->pick[ent][t] : __ldcg(a.ent_pick + ent * kTokPerEnt + t);
+    const float wt = tb ? tb->w[ent][t] : __ldcg(a.ent_w + ent * kTokPerEnt + t);
     float v[4] = {v_in[0], v_in[1], v_in[2], v_in[3]};
     fwht128_warp(v, lane);
     float4 yv;
@@ -591,13 +715,14 @@ __device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, 
     int oc = 0;
     if (lane == 0) oc = atomicAdd(&a.cnt_c[mt * nbH + nbh], 1);
     oc = __shfl_sync(0xffffffffu, oc, 0);
-    if (oc == __ldcg(a.tok_cnt + mt) - 1) {
+    const int tcnt = tb ? (int)tb->tok_cnt[mt] : __ldcg(a.tok_cnt + mt);
+    if (oc == tcnt - 1) {
         __threadfence();
         float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
         for (int k = 0; k < a.topk; ++k) {
             int pp = mt * a.topk + k;
-            if (!__ldcg(a.pick_act + pp)) continue;
+            if (!(tb ? (int)tb->act[pp] : __ldcg(a.pick_act + pp))) continue;
             float4 q4 = __ldcg(reinterpret_cast<const float4*>(a.y + (size_t)pp * a.H + nbh * 128 + 4 * lane));
             sm[0] += q4.x; sm[1] += q4.y; sm[2] += q4.z; sm[3] += q4.w;
         }
@@ -670,11 +795,12 @@ __device__ __forceinline__ void copy_fills(const DecodeArgs& a) {
 // read of abuf.
 template <int KFIX, int PHASE>
 __device__ __forceinline__ void run_units(const DecodeArgs& a, int u0, int ustep, int nu, uint32_t* ring, uint32_t* side,
-                                          __half* xs, float acc[8][4], const LaneK<KFIX ? KFIX : 3>& lkf, bool wait_pdl) {
+                                          __half* xs, float acc[8][4], const LaneK<KFIX ? KFIX : 3>& lkf, bool wait_pdl,
+                                          const SmallTab* tb) {
     using C = StreamCfg<KFIX, PHASE>;
     static_assert(8 % kStages == 0, "ring slots must repeat every unit");
     const int lane = threadIdx.x & 31;
-    auto meta = [&](int i) { return load_meta<PHASE>(a, u0 + i * ustep, i < nu ? 0x7FFFFFFF : 0); };
+    auto meta = [&](int i) { return load_meta<PHASE>(a, u0 + i * ustep, i < nu ? 0x7FFFFFFF : 0, tb); };
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) acc[jj][0] = acc[jj][1] = acc[jj][2] = acc[jj][3] = 0.0f;
     UMeta mc = meta(0);
@@ -788,13 +914,25 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
     uint32_t* side = ring + kStages * C::STAGE;
     __half* xs = reinterpret_cast<__half*>(side + 2 * kSideWords);
     float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS);   // CTA sum [token][128]
+    SmallTab* tab = reinterpret_cast<SmallTab*>(part + kTokPerEnt * 128);
     LaneK<KFIX ? KFIX : 3> lkf;
     lkf.init(lane);
     const int cs = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
     const int cid = (int)blockIdx.x / cs, ncl = (int)gridDim.x / cs;
-    pdl_wait();
-    pdl_trigger();
-    const int n_ent = __ldcg(a.n_ent);
+    const SmallTab* tb = nullptr;
+    int n_ent;
+    if (a.small) {
+        // grouping in this CTA: no wait for the prep kernel until the cache fills (below)
+        pdl_trigger();
+        if (wid == 0) group_small(a, *tab);
+        __syncthreads();
+        tb = tab;
+        n_ent = tab->n;
+    } else {
+        pdl_wait();
+        pdl_trigger();
+        n_ent = __ldcg(a.n_ent);
+    }
     const int nKB = a.H / 128, nbI = a.I / 128;
     const int n_items = n_ent * nbI;
     const int half = cs / 2, upc = nKB / half;     // units per CTA, all of one projection
@@ -804,9 +942,10 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
         const int nu = upc > wid ? (upc - wid + 7) / 8 : 0;
         const int u0 = ((ent * 2 + proj) * nbI + nb) * nKB + kb0 + wid;
         GuEpi epi{};
-        if (rank == 0 && wid < __ldcg(a.ent_n + ent)) epi = gu_epi_load(a, ent, nb, wid);
+        const int ntok_e = tb ? (int)tb->ntok[ent] : __ldcg(a.ent_n + ent);
+        if (rank == 0 && wid < ntok_e) epi = gu_epi_load(a, ent, nb, wid, tb);
         float acc[8][4];
-        run_units<KFIX, 0>(a, u0, 8, nu, ring, side, xs, acc, lkf, false);
+        run_units<KFIX, 0>(a, u0, 8, nu, ring, side, xs, acc, lkf, false, tb);
         float* red = reinterpret_cast<float*>(ring);   // the warp's ring, side and xs are free now
         acc_to_smem(acc, red);
         __syncthreads();
@@ -818,8 +957,7 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
         }
         cluster_sync_all();
         if (rank == 0) {
-            const int ntok = __ldcg(a.ent_n + ent);
-            if (wid < ntok) {
+            if (wid < ntok_e) {
                 float g[4], u[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -836,7 +974,9 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
         cluster_sync_all();   // rank 0 has read every CTA's sums before they are overwritten or the CTAs exit
     }
     // cache fills are read by no kernel of this call (picks of a filled expert read its host copy until the commit
-    // at the end of the down phase): copied after the items, off the decode's critical path
+    // at the end of the down phase): copied after the items, off the decode's critical path (small batches wait for
+    // the cache step here, whose fill list they need)
+    if (a.small) pdl_wait();
     copy_fills(a);
 }
 
@@ -850,9 +990,19 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
     uint32_t* ring = smem + wid * C::WARP_WORDS;
     float* red = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + wid * kTokPerEnt * 128;
     float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + 8 * kTokPerEnt * 128;
+    SmallTab* tab = reinterpret_cast<SmallTab*>(part + kTokPerEnt * 128);
     LaneK<KFIX ? KFIX : 3> lkf;
     lkf.init(lane);
-    const int n_ent = __ldcg(a.n_ent);   // prep finished before the gate-up kernel could let this one start
+    const SmallTab* tb = nullptr;
+    int n_ent;
+    if (a.small) {   // own grouping, as the gate-up kernel
+        if (wid == 0) group_small(a, *tab);
+        __syncthreads();
+        tb = tab;
+        n_ent = tab->n;
+    } else {
+        n_ent = __ldcg(a.n_ent);   // prep finished before the gate-up kernel could let this one start
+    }
     const int nKBd = a.I / 128, nbH = a.H / 128;
     const int n_items = n_ent * nbH;
     bool first = true;
@@ -861,7 +1011,7 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
         const int nu = nKBd > wid ? (nKBd - wid + 7) / 8 : 0;
         const int u0 = (ent * nbH + nbh) * nKBd + wid;
         float acc[8][4];
-        run_units<KFIX, 1>(a, u0, 8, nu, ring, nullptr, nullptr, acc, lkf, first);
+        run_units<KFIX, 1>(a, u0, 8, nu, ring, nullptr, nullptr, acc, lkf, first, tb);
         first = false;
         acc_to_smem(acc, red);
         __syncthreads();
@@ -872,12 +1022,12 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
             part[q] = sm;
         }
         __syncthreads();
-        const int ntok = __ldcg(a.ent_n + ent);
+        const int ntok = tb ? (int)tb->ntok[ent] : __ldcg(a.ent_n + ent);
         if (wid < ntok) {
             float v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) v[j] = part[wid * 128 + 4 * lane + j];
-            dn_token_epilogue(a, ent, nbh, wid, v);
+            dn_token_epilogue(a, ent, nbh, wid, v, tb);
         }
         __syncthreads();
     }
@@ -885,20 +1035,47 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
         pdl_wait();
         pdl_trigger();
     }
-    // the last block to finish commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386)
+    // the last block to finish commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386); for small
+    // batches it also writes the tier mask into ids / w (every kernel of the call has read them by now) and zeroes
+    // the rows of tokens without an active pick
     __syncthreads();
-    if (threadIdx.x == 0 && a.fill_list) {
-        __threadfence();
-        int old = atomicAdd(a.blocks_done, 1);
-        if (old == (int)gridDim.x - 1) {
+    __shared__ int sh_last_blk;
+    if (threadIdx.x == 0) {
+        int last = 0;
+        if (a.fill_list || a.small) {
             __threadfence();
+            last = atomicAdd(a.blocks_done, 1) == (int)gridDim.x - 1;
+        }
+        sh_last_blk = last;
+    }
+    __syncthreads();
+    if (!sh_last_blk) return;
+    __threadfence();
+    if (threadIdx.x == 0) {
+        if (a.fill_list) {
             const int nf = __ldcg(a.fill_list);
             for (int q = 0; q < nf; ++q) {
                 int e = __ldcg(a.fill_list + 1 + q);
                 a.ptrs[e] = __ldcg(a.fill + e);
                 a.fill[e] = 0;
             }
-            a.blocks_done[0] = 0;
+        }
+        a.blocks_done[0] = 0;
+    }
+    if (a.small) {
+        const int np = a.M * a.topk;
+        for (int i = threadIdx.x; i < np; i += blockDim.x)
+            if (tab->masked[i]) {
+                const_cast<int32_t*>(a.ids)[i] = tab->safe;
+                const_cast<float*>(a.w)[i] = 0.0f;
+            }
+        for (int m = 0; m < a.M; ++m) {
+            if (tab->tok_cnt[m] != 0) continue;
+            for (int c = threadIdx.x; c < a.H; c += blockDim.x) {
+                if (a.out_bf16 == 2) reinterpret_cast<float*>(a.out)[(long long)m * a.os + c] = 0.0f;
+                else if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)m * a.os + c] = __float2bfloat16(0.0f);
+                else reinterpret_cast<__half*>(a.out)[(long long)m * a.os + c] = __float2half(0.0f);
+            }
         }
     }
 }
@@ -933,7 +1110,7 @@ static WsLayout ws_layout(int M, int topk, int H, int I) {
 template <int KFIX>
 static int launch_gu(const DecodeArgs& a, int nclusters, int cs, cudaStream_t s) {
     using C = StreamCfg<KFIX, 0>;
-    constexpr int smem = C::SMEM_BYTES + kTokPerEnt * 128 * 4;
+    constexpr int smem = C::SMEM_BYTES + kTokPerEnt * 128 * 4 + (int)sizeof(SmallTab);
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -964,7 +1141,7 @@ static int launch_gu(const DecodeArgs& a, int nclusters, int cs, cudaStream_t s)
 template <int KFIX>
 static int launch_dn(const DecodeArgs& a, int grid, cudaStream_t s) {
     using C = StreamCfg<KFIX, 1>;
-    constexpr int smem = C::SMEM_BYTES + 9 * kTokPerEnt * 128 * 4;
+    constexpr int smem = C::SMEM_BYTES + 9 * kTokPerEnt * 128 * 4 + (int)sizeof(SmallTab);
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1012,6 +1189,7 @@ static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int6
     a.y = (float*)(b + L.off[14]);
     a.ent_blob = (long long*)(b + L.off[15]); a.ent_k = (int*)(b + L.off[16]); a.blocks_done = (int*)(b + L.off[17]);
     a.maxent = M * topk;
+    a.small = (M <= kTokPerEnt && M * topk <= kSmallPicks && !(ea && ea->prefetch)) ? 1 : 0;
     EnsureArgs none{};
     prof_record(0, s);
     cudaError_t e = launch_k(prep_kernel, dim3(1), dim3(1024), 0, s, ea ? *ea : none, a, ea ? 1 : 0);
@@ -1114,6 +1292,11 @@ extern "C" EXL3B_API int exl3b_moe_decode_cached(const void* x, int64_t x_stride
     int mf = max_fill < E ? max_fill : E;
     EnsureArgs ea{ids, w, M * topk, layer, E, S, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob,
                   hstride > 0 ? hstride : blob, fill_all, fill_list, mf, 0, nullptr, ram_res, ring, ring_cap, safe, vict};
+    // small batches: the decode kernels group the picks themselves and the tier mask is written back at the end
+    a.t_slot_of = slot_of + (int64_t)layer * E;
+    a.t_ram_res = ram_res ? ram_res + (int64_t)layer * E : nullptr;
+    a.t_safe = safe ? safe + layer : nullptr;
+    ea.defer_mask = (M <= kTokPerEnt && M * topk <= kSmallPicks) ? 1 : 0;
     int nvict = vict ? std::min(mf, M * topk) : 0;
     return run_decode(a, &ea, workspace, ws_bytes, (cudaStream_t)stream, vict, host_base, slot_base,
                       hstride > 0 ? hstride : blob, vict_ram_res, nvict);

@@ -46,6 +46,8 @@ struct EnsureArgs {
     const int64_t* host_base; int64_t slot_base; int64_t blob; int64_t hstride;
     int64_t* fill_all; int32_t* fill_list; int max_fill; int prefetch; int32_t* pf_slot;
     const uint8_t* ram_res; int32_t* ring; int ring_cap; const int32_t* safe; int32_t* vict;
+    int defer_mask = 0;   // 1: the masked picks' in-place (safe, 0) rewrite of ids / w is left to the caller's last
+                          // kernel (npairs <= 32); the step itself uses the masked ids
 };
 
 __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
@@ -55,11 +57,14 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     __shared__ int miss[1024];
     __shared__ int vslot[1024];
     __shared__ int hist[256];
+    __shared__ unsigned char s_msk[32];   // defer_mask: picks masked by step 1
     const int tid = threadIdx.x;
     const int E = a.E, S = a.S, L = a.layer;
     int total;
 
     // 1. tier mask, picks in ascending index
+    if (a.defer_mask)
+        for (int i = tid; i < 32; i += kEnsureThreads) s_msk[i] = 0;
     if (a.ram_res && !a.prefetch) {
         if (tid == 0) sh_base_ring = a.ring[0];
         __syncthreads();
@@ -74,8 +79,12 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
             if (flag) {
                 int c = sh_base_ring + pre;
                 a.ring[1 + (c % a.ring_cap)] = key;
-                a.ids[i] = a.safe[L];
-                a.w[i] = 0.0f;
+                if (a.defer_mask) {
+                    s_msk[i] = 1;
+                } else {
+                    a.ids[i] = a.safe[L];
+                    a.w[i] = 0.0f;
+                }
             }
             __syncthreads();
             if (tid == 0) sh_base_ring += total;
@@ -88,7 +97,7 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     for (int e = tid; e < E; e += kEnsureThreads) need[e] = 0;
     __syncthreads();
     for (int i = tid; i < a.npairs; i += kEnsureThreads) {
-        int e = a.ids[i];
+        int e = (a.defer_mask && s_msk[i]) ? a.safe[L] : a.ids[i];
         if (e >= 0 && e < E) need[e] = 1;
         else set_error(kErrBounds);
     }

@@ -12,11 +12,12 @@
 
 namespace exl3b {
 
-// One warp per token: top-k by repeated warp argmax (ties -> lower id), then the renormalised softmax.
-__device__ __forceinline__ void topk_warp(const float* __restrict__ logits, int t, int E, int topk, int* __restrict__ ids,
-                                          float* __restrict__ w) {
+// One warp per token: top-k by repeated warp argmax (ties -> lower id), then the renormalised softmax.  MAXJ values
+// per lane (E <= 32 MAXJ): instantiated for E <= 512 (16) and E <= 1024 (32).
+template <int MAXJ>
+__device__ __forceinline__ void topk_warp_n(const float* __restrict__ logits, int t, int E, int topk,
+                                            int* __restrict__ ids, float* __restrict__ w) {
     const int lane = threadIdx.x & 31;
-    constexpr int MAXJ = 32;   // E <= 1024
     float v[MAXJ];
     const int nj = (E + 31) / 32;
 #pragma unroll
@@ -53,6 +54,12 @@ __device__ __forceinline__ void topk_warp(const float* __restrict__ logits, int 
         ids[(long long)t * topk + lane] = se;
         w[(long long)t * topk + lane] = ex / ssum;
     }
+}
+
+__device__ __forceinline__ void topk_warp(const float* __restrict__ logits, int t, int E, int topk,
+                                          int* __restrict__ ids, float* __restrict__ w) {
+    if (E <= 512) topk_warp_n<16>(logits, t, E, topk, ids, w);
+    else topk_warp_n<32>(logits, t, E, topk, ids, w);
 }
 
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, int topk,

@@ -60,7 +60,7 @@ def test_blob_dequant_mixed_k():
 
 
 # ------------------------------------------------------------------------------------------------ router
-@pytest.mark.parametrize("T", [1, 4, 33])
+@pytest.mark.parametrize("T", [1, 3, 4, 5, 8, 33])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_router_bit_exact(T, with_bias):
     H, E, topk = 2048, 512, 10
@@ -71,6 +71,25 @@ def test_router_bit_exact(T, with_bias):
     rid, rw, _ = O.router(bits(x), bits(wr), bias.numpy() if bias is not None else None, topk)
     assert np.array_equal(ids.cpu().numpy(), rid)
     assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("T", [1, 6, 12])
+def test_router_ties_to_lower_id(T):
+    """Duplicated router rows give exactly equal logits: the lower expert id is selected first."""
+    H, E, topk = 2048, 512, 10
+    x = synth.activations(T, H, 300 + T)
+    wr = synth.router_weight(E, H, 0.02, 9)
+    wr[256:] = wr[:256]
+    ids, w = X.router_topk(x.to(DEV), wr.to(DEV), None, topk)
+    rid, rw, _ = O.router(bits(x), bits(wr), None, topk)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
+    idn = ids.cpu().numpy()
+    for row in idn:   # every pair (e, e + 256) appears with the lower id first
+        pos = {int(e): i for i, e in enumerate(row)}
+        for e in pos:
+            if e < 256 and e + 256 in pos:
+                assert pos[e] < pos[e + 256]
 
 
 # ------------------------------------------------------------------------------------------------ decode layer
