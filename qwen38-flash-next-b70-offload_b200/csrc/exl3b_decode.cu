@@ -318,93 +318,68 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
     return true;
 }
 
-// One warp groups a small batch into tb (the caller synchronises the block afterwards): the same entries, pick
-// order and token counts as prep's grouping after the tier mask, computed from the call's ids / w (read from L2:
-// they were written by kernels before this one) and the read-only tier state.  Concurrent cache-state writes by the
-// prep kernel do not change the result: a miss keeps reading its host copy until the commit, and the mask of a
-// picked key does not depend on slot assignment.
+// One warp groups a small batch into tb (the caller synchronises the block afterwards): the same picks per expert
+// (in ascending pick index, at most kTokPerEnt per entry) and token counts as prep's grouping after the tier mask,
+// computed from the call's ids / w (read from L2: they were written by kernels before this one) and the read-only
+// tier state.  Entries are numbered in the order of their experts' first picks (prep numbers them by expert id; no
+// result depends on the order).  Concurrent cache-state writes by the prep kernel do not change the result: a miss
+// keeps reading its host copy until the commit, and the mask of a picked key does not depend on slot assignment.
 __device__ __forceinline__ void group_small(const DecodeArgs& a, SmallTab& tb) {
-    constexpr int J = kSmallPicks / 32;
+    static_assert(kSmallPicks == 32, "one pick per lane");
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int np = a.M * a.topk, E = a.E;
     const int kpack = a.K | (a.K << 4) | (a.K << 8);
     const bool tier = a.t_ram_res != nullptr && a.t_slot_of != nullptr && a.t_safe != nullptr;
+    // two dependent rounds of L2 loads: (ids, w, safe), then every table entry the pick may need (its own and the
+    // safe expert's), selected afterwards
     const int safe = tier ? __ldcg(a.t_safe) : 0;
-    int id[J], kv[J];
-    float wv[J];
-    long long pt[J];
-    bool act[J], msk[J];
+    int id = lane < np ? __ldcg(a.ids + lane) : -1;
+    float wv = lane < np ? __ldcg(a.w + lane) : 0.0f;
+    const bool safe_ok = tier && safe >= 0 && safe < E;
+    const long long p_safe = safe_ok ? (long long)__ldcg(a.ptrs + safe) : 0;
+    const int k_safe = (safe_ok && a.kinfo) ? __ldcg(a.kinfo + safe) : kpack;
+    const bool inr = id >= 0 && id < E;
+    const int so = (inr && tier) ? __ldcg(a.t_slot_of + id) : 0;
+    const int rr = (inr && tier) ? (int)__ldcg(a.t_ram_res + id) : 1;
+    long long pt = inr ? (long long)__ldcg(a.ptrs + id) : 0;
+    int kv = (inr && a.kinfo) ? __ldcg(a.kinfo + id) : kpack;
+    const bool msk = inr && tier && so < 0 && rr == 0;
+    if (msk) { id = safe; wv = 0.0f; pt = p_safe; kv = k_safe; }
+    const bool act = inr && !(msk && !safe_ok) && !(a.skip_zero && wv == 0.0f);
+    // lanes of the same expert; rank among them; entries of up to kTokPerEnt picks in order of first pick
+    const unsigned lt = (1u << lane) - 1u;
+    const unsigned grp = __match_any_sync(FULL, act ? id : -2 - lane);
+    const int sl = __popc(grp & lt), cnt = __popc(grp);
+    const int lead = __ffs(grp) - 1;
+    const bool first = act && sl == 0;
+    const int nent = first ? (cnt + kTokPerEnt - 1) / kTokPerEnt : 0;   // entries of the lead lane's expert
+    int base;   // entries before the expert's first one
+    if (__any_sync(FULL, nent > 1)) {
+        int x = nent;
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const int i = lane + 32 * j;
-        const bool val = i < np;
-        int e = val ? __ldcg(a.ids + i) : -1;
-        float ww = val ? __ldcg(a.w + i) : 0.0f;
-        const bool inr = e >= 0 && e < E;
-        msk[j] = false;
-        if (inr && tier && __ldcg(a.t_slot_of + e) < 0 && __ldcg(a.t_ram_res + e) == 0) {
-            msk[j] = true;
-            e = safe;
-            ww = 0.0f;
-        }
-        id[j] = e;
-        wv[j] = ww;
-        act[j] = inr && !(a.skip_zero && ww == 0.0f);
-        pt[j] = act[j] ? (long long)__ldcg(a.ptrs + e) : 0;
-        kv[j] = (act[j] && a.kinfo) ? __ldcg(a.kinfo + e) : kpack;
+        for (int o = 1; o < 32; o <<= 1) { const int y = __shfl_up_sync(FULL, x, o); if (lane >= o) x += y; }
+        base = __shfl_sync(FULL, x - nent, lead);
+    } else {
+        base = __popc(__ballot_sync(FULL, first) & ((1u << lead) - 1u));
     }
-    int sl[J], cnt[J], en[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) { sl[j] = 0; cnt[j] = 0; en[j] = 0; }
-#pragma unroll
-    for (int qj = 0; qj < J; ++qj) {
-        if (qj * 32 >= np) break;
-        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
-            const int eq = __shfl_sync(FULL, id[qj], ql);
-            const int aq = __shfl_sync(FULL, (int)act[qj], ql);
-#pragma unroll
-            for (int j = 0; j < J; ++j)
-                if (act[j] && aq && eq == id[j]) {
-                    ++cnt[j];
-                    if (qj * 32 + ql < lane + 32 * j) ++sl[j];
-                }
+    const int ndist = __reduce_add_sync(FULL, (unsigned)nent);
+    if (lane < kSmallPicks) { tb.act[lane] = act ? 1 : 0; tb.masked[lane] = msk ? 1 : 0; }
+    if (act) {
+        const int en = base + sl / kTokPerEnt, q = sl % kTokPerEnt;
+        const int nt = min(kTokPerEnt, cnt - (sl / kTokPerEnt) * kTokPerEnt);
+        if (q == 0) {
+            tb.blob[en] = pt;
+            tb.kv[en] = kv;
+            tb.ntok[en] = (unsigned char)nt;
+            for (int r = nt; r < kTokPerEnt; ++r) { tb.tok[en][r] = 0; tb.pick[en][r] = 0; tb.w[en][r] = 0.0f; }
         }
-    }
-    int ndist = 0;
-#pragma unroll
-    for (int qj = 0; qj < J; ++qj) {
-        if (qj * 32 >= np) break;
-        const bool first_q = act[qj] && sl[qj] == 0;
-        ndist += __popc(__ballot_sync(FULL, first_q));
-        for (int ql = 0; ql < 32 && qj * 32 + ql < np; ++ql) {
-            const int eq = __shfl_sync(FULL, id[qj], ql);
-            const int fq = __shfl_sync(FULL, (int)first_q, ql);
-#pragma unroll
-            for (int j = 0; j < J; ++j)
-                if (fq && eq < id[j]) ++en[j];
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const int i = lane + 32 * j;
-        if (i < kSmallPicks) { tb.act[i] = act[j] ? 1 : 0; tb.masked[i] = msk[j] ? 1 : 0; }
-        if (!act[j]) continue;
-        if (sl[j] == 0) {
-            tb.blob[en[j]] = pt[j];
-            tb.kv[en[j]] = kv[j];
-            tb.ntok[en[j]] = (unsigned char)cnt[j];
-            for (int q = cnt[j]; q < kTokPerEnt; ++q) { tb.tok[en[j]][q] = 0; tb.pick[en[j]][q] = 0; tb.w[en[j]][q] = 0.0f; }
-        }
-        tb.tok[en[j]][sl[j]] = (unsigned char)(i / a.topk);
-        tb.pick[en[j]][sl[j]] = (unsigned char)i;
-        tb.w[en[j]][sl[j]] = wv[j];
+        tb.tok[en][q] = (unsigned char)(lane / a.topk);
+        tb.pick[en][q] = (unsigned char)lane;
+        tb.w[en][q] = wv;
     }
     for (int m = 0; m < a.M; ++m) {
-        int c = 0;
-#pragma unroll
-        for (int j = 0; j < J; ++j) c += (act[j] && (lane + 32 * j) / a.topk == m) ? 1 : 0;
-        c = __reduce_add_sync(FULL, (unsigned)c);
+        const int c = __popc(__ballot_sync(FULL, act && lane / a.topk == m));
         if (lane == 0) tb.tok_cnt[m] = (unsigned char)c;
     }
     if (lane == 0) { tb.n = ndist; tb.safe = safe; }
@@ -439,10 +414,10 @@ __global__ void __launch_bounds__(1024) prep_kernel(EnsureArgs ea, DecodeArgs da
 
 // ------------------------------------------------------------------------------------------------ streaming core
 // Each warp streams its units' 8-tile strips row by row through a private SMEM ring filled with cp.async (16 B,
-// L2-only), kStages rows ahead of the decode.  A strip row is 2 PLANAR4 groups; in SMEM each plane of a group is
+// L2-only), NST - 1 rows ahead of the decode.  A strip row is 2 PLANAR4 groups; in SMEM each plane of a group is
 // padded to 4G + 8 words (D > 1), so the two words a lane reads per tile -- word (tile j, period g, plane i) at
 // i*PS + j*G + g -- fall in distinct banks across the warp.  Unit metadata is loaded one unit ahead.
-constexpr int kStages = 4;   // divides the 8 rows of a unit: ring slots are compile-time per row
+constexpr int kStages = 4;   // ring rows of gate-up (and of down for K = 5); divides the 8 rows of a unit
 
 __device__ __forceinline__ void cp_async16(uint32_t* smem, const void* gmem) {
     unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -490,17 +465,22 @@ struct LaneK {
 constexpr int kRowMaxWords = 2 * 5 * (4 * 8 + 8);   // Ring<5>::ROWW, the largest strip row of K in 2..5
 constexpr int kSideWords = 64 + kTokPerEnt * 64;      // gate-up: suh block (128 fp16) + x block of 8 tokens
 constexpr int kXsStride = 136;                        // xh row stride (fp16): rows of different tokens hit other banks
+static_assert(kTokPerEnt * kXsStride * 2 <= kTokPerEnt * 128 * 4, "down B operand fits the warp's accumulator area");
 
 template <int KFIX, int PHASE>
 struct StreamCfg {
     static constexpr int ROWW = KFIX ? Ring<KFIX>::ROWW : kRowMaxWords;
     static constexpr int STAGE = ROWW;
-    static constexpr int WARP_WORDS = kStages * STAGE + (PHASE == 0 ? 2 * kSideWords + kTokPerEnt * kXsStride / 2 : 0);
+    // down with rows of <= 1 KB keeps a whole unit in flight: its CTAs issue 7 of the 8 rows before they wait for
+    // the gate-up kernel, so that only the decode is left once abuf is ready
+    static constexpr int NST = (PHASE == 1 && ROWW <= 256) ? 8 : kStages;
+    static constexpr int WARP_WORDS = NST * STAGE + (PHASE == 0 ? 2 * kSideWords + kTokPerEnt * kXsStride / 2 : 0);
     static constexpr int SMEM_BYTES = 8 * WARP_WORDS * 4;
 };
 
 struct UMeta {
-    int valid, ent, f0, f1, f2, K, kv, ntok, tok, pick;   // f0..f2: (proj, nb, kb) gate-up; (nbh, kbi, -) down
+    int valid, ent, f0, f1, f2, K, kv, ntok, tok, pick;   // f0..f2: (proj, nb, kb) gate-up; (nbh, first row, -) down
+    int nr;                // strip rows of the unit: 8 (gate-up), 1..8 (down)
     const uint8_t* blob;
     const uint32_t* src;   // first word of the unit's strip (row 0)
     int rs;                // words between strip rows
@@ -513,7 +493,7 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
     m.valid = u < n_units;
     if (!m.valid) {
         m.ent = 0; m.f0 = m.f1 = m.f2 = 0; m.K = 3; m.kv = 0; m.ntok = 0; m.tok = 0; m.pick = 0; m.blob = nullptr;
-        m.src = nullptr; m.rs = 0;
+        m.src = nullptr; m.rs = 0; m.nr = 0;
         return m;
     }
     if (PHASE == 0) {
@@ -521,9 +501,15 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
         m.f2 = u % nKB; int r = u / nKB;
         m.f1 = r % nbI; r /= nbI;
         m.f0 = r & 1; m.ent = r >> 1;
+        m.nr = 8;
     } else {
-        const int nKBd = a.I / 128, nbH = a.H / 128;
-        m.f1 = u % nKBd; int r = u / nKBd;
+        // down unit u = ((ent nbH + nbh) 8 + w) nch + c: chunk c (<= 8 rows) of warp w's rows [w R, (w + 1) R) of the
+        // item's I/16 strip rows, R = I/128
+        const int R = a.I / 128, nch = (R + 7) / 8, nbH = a.H / 128;
+        const int c = u % nch; int r = u / nch;
+        const int w = r % 8; r /= 8;
+        m.f1 = w * R + 8 * c;
+        m.nr = min(8, R - 8 * c);
         m.f0 = r % nbH; m.ent = r / nbH; m.f2 = 0;
     }
     if (tb) {
@@ -547,7 +533,7 @@ __device__ __forceinline__ UMeta load_meta(const DecodeArgs& a, int u, int n_uni
         m.src = words + (size_t)(m.f2 * 8) * m.rs + (m.f0 ? (size_t)(a.I / 16) * 8 * gm.Kg : 0) + (size_t)(m.f1 * 2) * 4 * 8 * m.K;
     } else {
         m.rs = (int)gm.d_row_words();
-        m.src = words + gm.gu_words() + (size_t)(m.f1 * 8) * m.rs + (size_t)(m.f0 * 2) * 4 * 8 * m.K;
+        m.src = words + gm.gu_words() + (size_t)m.f1 * m.rs + (size_t)(m.f0 * 2) * 4 * 8 * m.K;
     }
     return m;
 }
@@ -644,6 +630,14 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, long long o, cons
 // abuf = fp16(FWHT(a) r).
 // The lane's scale vectors (svh_g, svh_u, suh_d: 4 fp16 each at columns 4 lane..) and the token's pick index, loaded
 // before the item's decode so that the epilogue waits on no global load.
+// Non-coherent 8-byte load issued where it stands (volatile: not sunk to its first use), so that the scale vectors
+// of an item's epilogue are in flight during the item's decode.
+__device__ __forceinline__ uint2 ldg_early(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
 struct GuEpi {
     uint2 svg, svu, sud;
     int pick;
@@ -653,10 +647,11 @@ __device__ __forceinline__ GuEpi gu_epi_load(const DecodeArgs& a, int ent, int n
     const int kv = tb ? tb->kv[ent] : __ldcg(a.ent_k + ent);
     const uint8_t* blob = reinterpret_cast<const uint8_t*>(tb ? tb->blob[ent] : __ldcg(a.ent_blob + ent));
     const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
+    const size_t col = (size_t)(nb * 128 + 4 * lane) * 2;
     GuEpi q;
-    q.svg = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_g()) + nb * 128 + 4 * lane));
-    q.svu = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_svh_u()) + nb * 128 + 4 * lane));
-    q.sud = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(blob + gm.off_suh_d()) + nb * 128 + 4 * lane));
+    q.svg = ldg_early(blob + gm.off_svh_g() + col);
+    q.svu = ldg_early(blob + gm.off_svh_u() + col);
+    q.sud = ldg_early(blob + gm.off_suh_d() + col);
     q.pick = tb ? tb->pick[ent][t] : __ldcg(a.ent_pick + ent * kTokPerEnt + t);
     return q;
 }
@@ -691,14 +686,19 @@ __device__ __forceinline__ void gu_token_epilogue(const DecodeArgs& a, const GuE
 
 // Down (:355-364): y = FWHT(v) (r w) svh_d (fp32); then the combine (:387-394) of the token's 128-block by the last
 // of its active picks to finish: out[m] = sum_k y[m,k] in fixed k order.
-__device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, int nbh, int t, const float v_in[4],
-                                                  const SmallTab* tb) {
+__device__ __forceinline__ uint2 dn_epi_load(const DecodeArgs& a, int ent, int nbh, const SmallTab* tb) {
     const int lane = threadIdx.x & 31;
-    const int nbH = a.H / 128;
     const int kv = tb ? tb->kv[ent] : __ldcg(a.ent_k + ent);
     const uint8_t* blob = reinterpret_cast<const uint8_t*>(tb ? tb->blob[ent] : __ldcg(a.ent_blob + ent));
     const Geom gm{a.H, a.I, kv & 15, (kv >> 4) & 15, (kv >> 8) & 15};
-    const __half* svd = reinterpret_cast<const __half*>(blob + gm.off_svh_d()) + nbh * 128 + 4 * lane;
+    return ldg_early(blob + gm.off_svh_d() + (size_t)(nbh * 128 + 4 * lane) * 2);
+}
+
+__device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, int nbh, int t, const float v_in[4],
+                                                  const SmallTab* tb, const uint2 v_svd) {
+    const int lane = threadIdx.x & 31;
+    const int nbH = a.H / 128;
+    const __half* svd = reinterpret_cast<const __half*>(&v_svd);
     const int pick = tb ? tb->pick[ent][t] : __ldcg(a.ent_pick + ent * kTokPerEnt + t);
     const float wt = tb ? tb->w[ent][t] : __ldcg(a.ent_w + ent * kTokPerEnt + t);
     float v[4] = {v_in[0], v_in[1], v_in[2], v_in[3]};
@@ -790,7 +790,7 @@ __device__ __forceinline__ void copy_fills(const DecodeArgs& a) {
 }
 
 // Stream a warp's units (unit ids u0, u0 + ustep, ... : nu of them, all of one item) row by row through the warp's
-// SMEM ring (kStages rows in flight, rows unrolled so every ring slot is fixed) and accumulate W^T B over all of them
+// SMEM ring (C::NST - 1 rows in flight, rows unrolled so every ring slot is fixed) and accumulate W^T B over all of them
 // into acc.  PHASE 1 waits for the previous kernel (wait_pdl) after the ring prologue is issued, before its first
 // read of abuf.
 template <int KFIX, int PHASE>
@@ -798,7 +798,8 @@ __device__ __forceinline__ void run_units(const DecodeArgs& a, int u0, int ustep
                                           __half* xs, float acc[8][4], const LaneK<KFIX ? KFIX : 3>& lkf, bool wait_pdl,
                                           const SmallTab* tb) {
     using C = StreamCfg<KFIX, PHASE>;
-    static_assert(8 % kStages == 0, "ring slots must repeat every unit");
+    constexpr int NST = C::NST;
+    static_assert(8 % NST == 0, "ring slots must repeat every unit");
     const int lane = threadIdx.x & 31;
     auto meta = [&](int i) { return load_meta<PHASE>(a, u0 + i * ustep, i < nu ? 0x7FFFFFFF : 0, tb); };
 #pragma unroll
@@ -806,8 +807,8 @@ __device__ __forceinline__ void run_units(const DecodeArgs& a, int u0, int ustep
     UMeta mc = meta(0);
     if (mc.valid) {
 #pragma unroll
-        for (int r = 0; r < kStages - 1; ++r) {
-            issue_any<KFIX, PHASE>(a, mc, r, ring + r * C::STAGE, side, lkf);
+        for (int r = 0; r < NST - 1; ++r) {
+            if (PHASE == 0 || r < mc.nr) issue_any<KFIX, PHASE>(a, mc, r, ring + r * C::STAGE, side, lkf);
             cp_commit();
         }
     }
@@ -816,44 +817,38 @@ __device__ __forceinline__ void run_units(const DecodeArgs& a, int u0, int ustep
         pdl_trigger();
     }
     const int tk = lane >> 2, kq = 2 * (lane & 3);
-    auto load_b = [&](const UMeta& m, int r, uint32_t& b0, uint32_t& b1) {
-        const int pk = __shfl_sync(0xffffffffu, m.pick, tk);
-        if (tk < m.ntok) {
-            const __half* ar = a.abuf + (size_t)pk * a.I + m.f1 * 128 + r * 16 + kq;
-            b0 = __ldcg(reinterpret_cast<const unsigned int*>(ar));
-            b1 = __ldcg(reinterpret_cast<const unsigned int*>(ar + 8));
-        } else {
-            b0 = b1 = 0u;
-        }
-    };
-    uint32_t nb0 = 0, nb1 = 0;   // down: B operand of the next row, loaded one row ahead
-    if (PHASE == 1 && mc.valid) load_b(mc, 0, nb0, nb1);
     for (int i = 0; i < nu; ++i) {
         const UMeta mn = meta(i + 1);
         uint32_t* sd = side + (i & 1) * kSideWords;
         uint32_t* sdn = side + ((i + 1) & 1) * kSideWords;
+        if (PHASE == 1) {
+            // down: the unit's B operand (the unit's 16 nr k-values of each token's abuf row, written by the gate-up
+            // kernel) into xs, one L2 round trip per unit instead of one per row (plain loads: the ring's copy groups
+            // stay in flight)
+            for (int c0 = 0; c0 < 16 * mc.ntok; c0 += 32) {   // uniform trip count: the shuffle sees every lane
+                const int c = c0 + lane, t = (c >> 4) & 7, j = c & 15;
+                const int pk = __shfl_sync(0xffffffffu, mc.pick, t);
+                if (c < 16 * mc.ntok && j < 2 * mc.nr)
+                    *reinterpret_cast<uint4*>(xs + t * kXsStride + j * 8) =
+                        __ldcg(reinterpret_cast<const uint4*>(a.abuf + (size_t)pk * a.I + mc.f1 * 16 + j * 8));
+            }
+            __syncwarp();
+        }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
-            constexpr int L = kStages - 1;
+            constexpr int L = NST - 1;
             const int rr = r + L;   // row issued now: of this unit, or (rr >= 8) of the next one
-            if (rr < 8) issue_any<KFIX, PHASE>(a, mc, rr, ring + (rr % kStages) * C::STAGE, sd, lkf);
-            else if (mn.valid) issue_any<KFIX, PHASE>(a, mn, rr - 8, ring + (rr % kStages) * C::STAGE, sdn, lkf);
+            // a unit of fewer than 8 rows is its warp's last: nothing follows it
+            if (rr < 8) { if (PHASE == 0 || rr < mc.nr) issue_any<KFIX, PHASE>(a, mc, rr, ring + (rr % NST) * C::STAGE, sd, lkf); }
+            else if (mn.valid && (PHASE == 0 || rr - 8 < mn.nr)) issue_any<KFIX, PHASE>(a, mn, rr - 8, ring + (rr % NST) * C::STAGE, sdn, lkf);
             cp_commit();
-            cp_wait<kStages - 1>();
+            cp_wait<NST - 1>();
             __syncwarp();
-            const uint32_t* stage = ring + (r % kStages) * C::STAGE;
+            const uint32_t* stage = ring + (r % NST) * C::STAGE;
             if (PHASE == 0 && r == 0) unit_xh(a, mc, sd, xs);
-            uint32_t b0, b1;
-            if (PHASE == 0) {
-                b0 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq);
-                b1 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq + 8);
-            } else {
-                b0 = nb0;
-                b1 = nb1;
-                if (r < 7) load_b(mc, r + 1, nb0, nb1);
-                else if (mn.valid) load_b(mn, 0, nb0, nb1);
-            }
-            consume_any<KFIX>(mc.K, stage, b0, b1, acc, lkf);
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xs + tk * kXsStride + r * 16 + kq + 8);
+            if (PHASE == 0 || r < mc.nr) consume_any<KFIX>(mc.K, stage, b0, b1, acc, lkf);
             __syncwarp();
         }
         mc = mn;
@@ -891,34 +886,42 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
-// Load from the shared memory of CTA `rank` of this cluster at the address this CTA uses for `p`.
-__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+// Store to the shared memory of CTA `rank` of this cluster at the address this CTA uses for `p`.
+__device__ __forceinline__ void st_dsmem(float* p, uint32_t rank, float v) {
     uint32_t la = (uint32_t)__cvta_generic_to_shared(p), ra;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
 // Gate-up: a cluster of cs CTAs (4, or 2 when H/128 is odd) per item (entry, 128-column block of I).  The item's
 // 2 H/128 units (proj, 128-row k-block) are split evenly: CTA rank r takes units of projection r / (cs/2), k-blocks
 // (r % (cs/2)) * upc + w + 8 j for its warp w.  Each CTA sums its warps' accumulators in shared memory (fixed
-// order); rank 0 adds the CTAs' sums of each projection (fixed rank order, read over DSMEM) and runs the epilogue,
-// one warp per token.  Items are dealt to clusters round-robin; no global partials, no atomics.
+// order); CTAs r > 0 store the sums of the item's tokens into rank 0's gather slot r - 1 (DSMEM), rank 0 keeps its
+// own in place.  After one cluster barrier rank 0 adds the sums of each projection in rank order and runs the
+// epilogue, one warp per token.  Items are dealt to clusters round-robin; no global partials, no atomics.
+// Dynamic shared memory: 8 warp areas, the gather slots ((cs - 1) x min(M, 8) tokens x 128 fp32), the small-batch
+// table.
+__host__ __device__ constexpr int gu_gather_tokens(int M) { return M < 1 ? 1 : (M < kTokPerEnt ? M : kTokPerEnt); }
+__host__ __device__ constexpr int gu_gather_floats(int cs, int M) { return (cs - 1) * gu_gather_tokens(M) * 128; }
+
 template <int KFIX>
 __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
     using C = StreamCfg<KFIX, 0>;
     extern __shared__ __align__(16) uint32_t smem[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     uint32_t* ring = smem + wid * C::WARP_WORDS;
-    uint32_t* side = ring + kStages * C::STAGE;
+    uint32_t* side = ring + C::NST * C::STAGE;
     __half* xs = reinterpret_cast<__half*>(side + 2 * kSideWords);
-    float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS);   // CTA sum [token][128]
-    SmallTab* tab = reinterpret_cast<SmallTab*>(part + kTokPerEnt * 128);
+    const int mt = gu_gather_tokens(a.M);   // tokens per gather slot
+    float* gather = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS);   // rank 0: slots [rank - 1][token][128]
+    SmallTab* tab = reinterpret_cast<SmallTab*>(gather + gu_gather_floats((int)cluster_nctarank(), a.M));
     LaneK<KFIX ? KFIX : 3> lkf;
     lkf.init(lane);
     const int cs = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
     const int cid = (int)blockIdx.x / cs, ncl = (int)gridDim.x / cs;
+    // every CTA of the cluster has started before the first DSMEM store: arrive now, wait before that store
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    bool cl_wait = true;
     const SmallTab* tb = nullptr;
     int n_ent;
     if (a.small) {
@@ -947,32 +950,41 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
         float acc[8][4];
         run_units<KFIX, 0>(a, u0, 8, nu, ring, side, xs, acc, lkf, false, tb);
         float* red = reinterpret_cast<float*>(ring);   // the warp's ring, side and xs are free now
-        acc_to_smem(acc, red);
-        __syncthreads();
-        for (int q = threadIdx.x; q < kTokPerEnt * 128; q += 256) {
-            float sm = 0.0f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) sm += reinterpret_cast<const float*>(smem + w * C::WARP_WORDS)[q];
-            part[q] = sm;
+        const int nwu = upc < 8 ? upc : 8;             // warps with units
+        if (wid < nwu) acc_to_smem(acc, red);
+        if (cl_wait) {
+            asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+            cl_wait = false;
         }
-        cluster_sync_all();
-        if (rank == 0) {
-            if (wid < ntok_e) {
-                float g[4], u[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float* pe = part + wid * 128 + 4 * lane + j;
-                    float gs = 0.0f, us = 0.0f;
-                    for (int r = 0; r < half; ++r) gs += ld_dsmem(pe, r);
-                    for (int r = half; r < cs; ++r) us += ld_dsmem(pe, r);
-                    g[j] = gs;
-                    u[j] = us;
+        __syncthreads();
+        // the gather slots hold mt tokens: an entry holds up to kTokPerEnt picks, more than mt only when a token
+        // picks one expert several times; such entries go through the slots in chunks of mt tokens
+        for (int t0 = 0; t0 < ntok_e; t0 += mt) {
+            const int nt = min(mt, ntok_e - t0);
+            for (int q = t0 * 128 + threadIdx.x; q < (t0 + nt) * 128; q += 256) {
+                float sm = 0.0f;
+                for (int w = 0; w < nwu; ++w) sm += reinterpret_cast<const float*>(smem + w * C::WARP_WORDS)[q];
+                if (rank == 0) reinterpret_cast<float*>(smem)[q] = sm;   // in place: this thread alone reads index q
+                else st_dsmem(gather + (rank - 1) * (mt * 128) + (q - t0 * 128), 0, sm);
+            }
+            cluster_sync_all();   // release / acquire: the gather slots are visible to rank 0; this CTA's reads of
+                                  // the warps' sums are done before the next item reuses the rings
+            if (rank == 0 && wid >= t0 && wid < t0 + nt) {
+                float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int r = 0; r < cs; ++r) {
+                    const float* src = r == 0 ? reinterpret_cast<const float*>(smem) + wid * 128
+                                              : gather + (r - 1) * (mt * 128) + (wid - t0) * 128;
+                    const float4 s4 = *reinterpret_cast<const float4*>(src + 4 * lane);
+                    float* d = r < half ? g : u;
+                    d[0] += s4.x; d[1] += s4.y; d[2] += s4.z; d[3] += s4.w;
                 }
                 gu_token_epilogue(a, epi, nb, g, u);
             }
+            // rank 0 has read the gather slots before the cluster's next chunk or item overwrites them
+            if (t0 + mt < ntok_e || item + ncl < n_items) cluster_sync_all();
         }
-        cluster_sync_all();   // rank 0 has read every CTA's sums before they are overwritten or the CTAs exit
     }
+    if (cl_wait) asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
     // cache fills are read by no kernel of this call (picks of a filled expert read its host copy until the commit
     // at the end of the down phase): copied after the items, off the decode's critical path (small batches wait for
     // the cache step here, whose fill list they need)
@@ -980,17 +992,18 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
     copy_fills(a);
 }
 
-// Down: one CTA per item (entry, 128-column block of H); warp w takes the k-blocks w + 8 j of the I/128 units.  The
-// first item's weight rows are issued before the wait for the gate-up kernel (only abuf depends on it).
+// Down: one CTA per item (entry, 128-column block of H); the item's I/16 strip rows are split evenly over the 8
+// warps (I/128 consecutive rows each).  The first item's weight rows are issued before the wait for the gate-up
+// kernel (only abuf depends on it).
 template <int KFIX>
 __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
     using C = StreamCfg<KFIX, 1>;
     extern __shared__ __align__(16) uint32_t smem[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     uint32_t* ring = smem + wid * C::WARP_WORDS;
-    float* red = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + wid * kTokPerEnt * 128;
-    float* part = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS) + 8 * kTokPerEnt * 128;
-    SmallTab* tab = reinterpret_cast<SmallTab*>(part + kTokPerEnt * 128);
+    float* red_all = reinterpret_cast<float*>(smem + 8 * C::WARP_WORDS);   // warps' accumulators [warp][token][128]
+    float* red = red_all + wid * kTokPerEnt * 128;
+    SmallTab* tab = reinterpret_cast<SmallTab*>(red_all + 8 * kTokPerEnt * 128);
     LaneK<KFIX ? KFIX : 3> lkf;
     lkf.init(lane);
     const SmallTab* tb = nullptr;
@@ -1005,48 +1018,53 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
     }
     const int nKBd = a.I / 128, nbH = a.H / 128;
     const int n_items = n_ent * nbH;
+    // The last block commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386); for small batches it
+    // also writes the tier mask into ids / w and zeroes the rows of tokens without an active pick.  A block arrives
+    // once it is past the wait for the gate-up kernel (the fills are copied, every other kernel of the call is done
+    // with ids / w and the table) and past its own grouping, i.e. after its first item's stream; the arrival's
+    // round trip then overlaps the item's epilogue.
+    __shared__ int sh_last_blk;
+    const bool need_last = a.fill_list || a.small;
+    auto arrive = [&]() {
+        if (threadIdx.x == 0) {
+            int last = 0;
+            if (need_last) {
+                __threadfence();
+                last = atomicAdd(a.blocks_done, 1) == (int)gridDim.x - 1;
+            }
+            sh_last_blk = last;
+        }
+    };
     bool first = true;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const int ent = item / nbH, nbh = item % nbH;
-        const int nu = nKBd > wid ? (nKBd - wid + 7) / 8 : 0;
-        const int u0 = (ent * nbH + nbh) * nKBd + wid;
+        const int nch = (nKBd + 7) / 8;   // the warp's I/128 strip rows, in units of up to 8
+        const int u0 = ((ent * nbH + nbh) * 8 + wid) * nch;
+        const int ntok = tb ? (int)tb->ntok[ent] : __ldcg(a.ent_n + ent);
+        uint2 svd = make_uint2(0u, 0u);
+        if (wid < ntok) svd = dn_epi_load(a, ent, nbh, tb);
         float acc[8][4];
-        run_units<KFIX, 1>(a, u0, 8, nu, ring, nullptr, nullptr, acc, lkf, first, tb);
+        // the warp's accumulator area holds the B operand during the stream (kTokPerEnt x kXsStride fp16 fit)
+        run_units<KFIX, 1>(a, u0, 1, nch, ring, nullptr, reinterpret_cast<__half*>(red), acc, lkf, first, tb);
+        if (first) arrive();
         first = false;
+        const int nwu = 8;   // every warp has I/128 >= 1 rows
         acc_to_smem(acc, red);
         __syncthreads();
-        for (int q = threadIdx.x; q < kTokPerEnt * 128; q += 256) {
-            float sm = 0.0f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) sm += reinterpret_cast<const float*>(smem + 8 * C::WARP_WORDS)[w * kTokPerEnt * 128 + q];
-            part[q] = sm;
-        }
-        __syncthreads();
-        const int ntok = tb ? (int)tb->ntok[ent] : __ldcg(a.ent_n + ent);
-        if (wid < ntok) {
-            float v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = part[wid * 128 + 4 * lane + j];
-            dn_token_epilogue(a, ent, nbh, wid, v, tb);
+        if (wid < ntok) {   // the token's warp sums the warps' accumulators in warp order
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int w = 0; w < nwu; ++w) {
+                const float4 s4 = *reinterpret_cast<const float4*>(red_all + (w * kTokPerEnt + wid) * 128 + 4 * lane);
+                v[0] += s4.x; v[1] += s4.y; v[2] += s4.z; v[3] += s4.w;
+            }
+            dn_token_epilogue(a, ent, nbh, wid, v, tb, svd);
         }
         __syncthreads();
     }
     if (first) {   // no item: still order this block after the gate-up kernel
         pdl_wait();
         pdl_trigger();
-    }
-    // the last block to finish commits the cache fills (CombineKernel item 0, exl3_moe.a8.sycl:378-386); for small
-    // batches it also writes the tier mask into ids / w (every kernel of the call has read them by now) and zeroes
-    // the rows of tokens without an active pick
-    __syncthreads();
-    __shared__ int sh_last_blk;
-    if (threadIdx.x == 0) {
-        int last = 0;
-        if (a.fill_list || a.small) {
-            __threadfence();
-            last = atomicAdd(a.blocks_done, 1) == (int)gridDim.x - 1;
-        }
-        sh_last_blk = last;
+        arrive();
     }
     __syncthreads();
     if (!sh_last_blk) return;
@@ -1110,12 +1128,13 @@ static WsLayout ws_layout(int M, int topk, int H, int I) {
 template <int KFIX>
 static int launch_gu(const DecodeArgs& a, int nclusters, int cs, cudaStream_t s) {
     using C = StreamCfg<KFIX, 0>;
-    constexpr int smem = C::SMEM_BYTES + kTokPerEnt * 128 * 4 + (int)sizeof(SmallTab);
+    constexpr int smem_max = C::SMEM_BYTES + gu_gather_floats(4, kTokPerEnt) * 4 + (int)sizeof(SmallTab);
+    const int smem = C::SMEM_BYTES + gu_gather_floats(cs, a.M) * 4 + (int)sizeof(SmallTab);
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(gu_cluster_kernel<KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gu_cluster_kernel<KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
         if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
         attr_dev = dev;
     }
@@ -1141,7 +1160,7 @@ static int launch_gu(const DecodeArgs& a, int nclusters, int cs, cudaStream_t s)
 template <int KFIX>
 static int launch_dn(const DecodeArgs& a, int grid, cudaStream_t s) {
     using C = StreamCfg<KFIX, 1>;
-    constexpr int smem = C::SMEM_BYTES + 9 * kTokPerEnt * 128 * 4 + (int)sizeof(SmallTab);
+    constexpr int smem = C::SMEM_BYTES + 8 * kTokPerEnt * 128 * 4 + (int)sizeof(SmallTab);
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);

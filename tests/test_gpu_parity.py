@@ -160,6 +160,17 @@ def test_zero_weight_picks_and_duplicates():
     assert torch.all(out[1].float() == 0)
 
 
+def test_small_batch_expert_with_more_than_eight_picks():
+    """One expert picked 10 times in a small batch (repeated within tokens): its picks span two entries of at most
+    8 tokens each, as in the grouped path."""
+    H, I, E, topk, K, T = 256, 128, 8, 4, 3, 3
+    blobs, ptrs, views = make_layer(E, H, I, K, seed=5)
+    x = synth.activations(T, H, 3)
+    ids = torch.tensor([[2, 2, 2, 2], [2, 2, 2, 2], [2, 4, 2, 6]], dtype=torch.int32)
+    w = torch.rand(T, topk, generator=torch.Generator().manual_seed(8)).float()
+    check_decode(x, ids, w, ptrs, views, H, I, K, E)
+
+
 def test_fp16_activations():
     H, I, E, topk, K, T = 256, 128, 8, 2, 3, 2
     blobs, ptrs, views = make_layer(E, H, I, K, seed=4)
