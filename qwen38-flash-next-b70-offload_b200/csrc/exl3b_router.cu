@@ -139,6 +139,116 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
     if (threadIdx.x == 0) *counter = 0;
 }
 
+// Large-T logits: a CUDA-core GEMM tile (64 tokens x 64 experts per block, 4 x 4 per thread) with the arithmetic
+// of router_logits_kernel bit for bit.  There, lane c sums chunk c (k in [c CL, (c + 1) CL)) in ascending k with fp32
+// fma from 0, and the xor butterfly (offsets 16, 8, 4, 2, 1) adds the 32 chunk sums as a fixed binary tree whose
+// leaves, left to right, are the chunks in 5-bit bit-reversed order (0, 16, 8, 24, 4, ...).  Here each thread
+// computes the chunk sums of its outputs in that order and folds each into a 5-level stack like a binary counter
+// (a left subtree waits at its level until its right sibling arrives: s = left + right), which forms the same tree.
+// Chunks pass through shared memory as fp32, [k][row] (double-buffered, loaded one chunk ahead).
+template <int CL>
+__global__ void __launch_bounds__(256, 1) router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
+                                                                     const __nv_bfloat16* __restrict__ wr,
+                                                                     const float* __restrict__ bias, int T, int H,
+                                                                     int E, float* __restrict__ logits) {
+    extern __shared__ __align__(16) float rsm[];
+    constexpr int NV = CL / 8;                     // 16-byte vectors per row of a chunk
+    constexpr int NLD = (64 * NV + 255) / 256;     // vectors per thread per operand
+    float* xsm = rsm;                              // [2][CL][64] tokens
+    float* wsm = rsm + 2 * CL * 64;                // [2][CL][64] experts
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+    uint4 rx[NLD], rw[NLD];
+    auto gload = [&](int c) {
+#pragma unroll
+        for (int q = 0; q < NLD; ++q) {
+            const int idx = tid + 256 * q, row = idx & 63, v = idx >> 6;
+            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+            const bool ok = idx < 64 * NV;
+            rx[q] = (ok && t0 + row < T) ? __ldg(reinterpret_cast<const uint4*>(x + (long long)(t0 + row) * xs + c * CL + v * 8)) : z;
+            rw[q] = (ok && e0 + row < E) ? __ldg(reinterpret_cast<const uint4*>(wr + (long long)(e0 + row) * H + c * CL + v * 8)) : z;
+        }
+    };
+    auto sstore = [&](int buf) {
+#pragma unroll
+        for (int q = 0; q < NLD; ++q) {
+            const int idx = tid + 256 * q, row = idx & 63, v = idx >> 6;
+            if (idx < 64 * NV) {
+                const uint32_t xw[4] = {rx[q].x, rx[q].y, rx[q].z, rx[q].w};
+                const uint32_t ww[4] = {rw[q].x, rw[q].y, rw[q].z, rw[q].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int kk = v * 8 + j;
+                    const uint32_t xb = (j & 1) ? (xw[j >> 1] & 0xFFFF0000u) : (xw[j >> 1] << 16);
+                    const uint32_t wb = (j & 1) ? (ww[j >> 1] & 0xFFFF0000u) : (ww[j >> 1] << 16);
+                    xsm[(buf * CL + kk) * 64 + row] = __uint_as_float(xb);
+                    wsm[(buf * CL + kk) * 64 + row] = __uint_as_float(wb);
+                }
+            }
+        }
+    };
+    pdl_wait();
+    pdl_trigger();
+    float st[5][16];   // left subtrees waiting at each level
+#pragma unroll
+    for (int l = 0; l < 5; ++l)
+#pragma unroll
+        for (int q = 0; q < 16; ++q) st[l][q] = 0.0f;
+    float sm[16];
+    gload(0);
+    sstore(0);
+    __syncthreads();
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i) {
+        if (i + 1 < 32) gload((int)(__brev((unsigned)(i + 1)) >> 27));
+        const float* xb = xsm + (i & 1) * CL * 64 + ty * 4;
+        const float* wb = wsm + (i & 1) * CL * 64 + tx * 4;
+        float pc[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) pc[q] = 0.0f;
+#pragma unroll 8
+        for (int kk = 0; kk < CL; ++kk) {
+            const float4 xv = *reinterpret_cast<const float4*>(xb + kk * 64);
+            const float4 wv = *reinterpret_cast<const float4*>(wb + kk * 64);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) pc[a * 4 + b] = __fmaf_rn(xa[a], wa[b], pc[a * 4 + b]);
+        }
+        bool carry = true;
+#pragma unroll
+        for (int l = 0; l < 5; ++l) {
+            if (carry) {
+                if ((i >> l) & 1) {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) pc[q] = __fadd_rn(st[l][q], pc[q]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) st[l][q] = pc[q];
+                    carry = false;
+                }
+            }
+        }
+        if (i == 31) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) sm[q] = pc[q];
+        }
+        if (i + 1 < 32) sstore((i + 1) & 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int t = t0 + ty * 4 + a;
+        if (t >= T) continue;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int e = e0 + tx * 4 + b;
+            if (e < E) __stcg(logits + (long long)t * E + e, bias ? __fadd_rn(sm[a * 4 + b], bias[e]) : sm[a * 4 + b]);
+        }
+    }
+}
+
 // Shared-expert gate (config 5): one warp per token; s = dot(x[t], g) with the router's arithmetic (lane c sums
 // chunk c in ascending k with fp32 fma, xor butterfly 16..1), weight = 1 / (1 + expf(-s)).  Writes the extended
 // routing [T][topk + 1]: the token's routed picks, then (shared_id, weight).
@@ -189,6 +299,10 @@ extern "C" EXL3B_API int exl3b_shared_gate(const void* x_bf16, int64_t x_stride,
     return 0;
 }
 
+// Token count from which the tiled logits kernel runs (below it, the warp-per-expert kernel's many small blocks are
+// faster).
+constexpr int kRouterTiledMinT = 128;
+
 extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias,
                                            int T, int H, int E, int topk, int32_t* ids, float* w, float* logits,
                                            int32_t* counter, void* stream) {
@@ -206,6 +320,28 @@ extern "C" EXL3B_API int exl3b_router_topk(const void* x_bf16, int64_t x_stride,
     const __nv_bfloat16* wp = (const __nv_bfloat16*)wr_bf16;
     int* ctr = (counter && T <= TC) ? counter : nullptr;   // fused selection when every token fits one block
     cudaError_t e = cudaSuccess;
+    if (T >= kRouterTiledMinT) {
+        const dim3 gt((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
+        const int CLv = H / 32;
+        const size_t smem = (size_t)4 * CLv * 64 * sizeof(float);
+        switch (CLv) {
+#define RT(CLV) case CLV: { \
+            static int attr_dev = -1; int dev = 0; cudaGetDevice(&dev); \
+            if (attr_dev != dev) { \
+                e = cudaFuncSetAttribute(router_logits_tiled_kernel<CLV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+                if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e)); \
+                attr_dev = dev; } \
+            e = launch_k(router_logits_tiled_kernel<CLV>, gt, dim3(256), smem, s, xp, x_stride, wp, bias, T, H, E, logits); \
+            break; }
+            RT(8) RT(16) RT(24) RT(32) RT(40) RT(48) RT(56) RT(64) RT(80) RT(96) RT(128)
+#undef RT
+            default: return exl3b_fail(EXL3B_EINVAL, "exl3b_router_topk: unsupported H");
+        }
+        if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+        e = launch_k(router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, (const float*)logits, T, E, topk, ids, w);
+        if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
+        return 0;
+    }
     switch (H / 32) {
 #define RL(CLV) case CLV: e = launch_k(router_logits_kernel<CLV, TC>, g1, dim3(256), 0, s, xp, x_stride, wp, bias, T, H, E, \
                                        logits, topk, ids, w, ctr); break;

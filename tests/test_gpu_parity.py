@@ -60,7 +60,7 @@ def test_blob_dequant_mixed_k():
 
 
 # ------------------------------------------------------------------------------------------------ router
-@pytest.mark.parametrize("T", [1, 3, 4, 5, 8, 33])
+@pytest.mark.parametrize("T", [1, 3, 4, 5, 8, 33, 200])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_router_bit_exact(T, with_bias):
     H, E, topk = 2048, 512, 10
@@ -73,7 +73,30 @@ def test_router_bit_exact(T, with_bias):
     assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
 
 
-@pytest.mark.parametrize("T", [1, 6, 12])
+@pytest.mark.parametrize("T", [128, 333])
+@pytest.mark.parametrize("H", [2048, 256])
+def test_router_logits_bit_exact_tiled(T, H):
+    """Token counts of the tiled logits kernel (partial 64-token tiles, a short chunk length at H=256): the logits
+    themselves match the oracle bit for bit, then the picks."""
+    E, topk = 512, 10
+    x = synth.activations(T, H, 700 + T)
+    wr = synth.router_weight(E, H, 0.02, 11)
+    bias = synth.zipf_bias(E, 3, 11)
+    xd, wd, bd = x.to(DEV), wr.to(DEV), bias.to(DEV)
+    ids = torch.empty((T, topk), dtype=torch.int32, device=DEV)
+    w = torch.empty((T, topk), dtype=torch.float32, device=DEV)
+    logits = torch.empty((T, E), dtype=torch.float32, device=DEV)
+    from exl3b200._lib import lib, check, stream
+    check(lib().exl3b_router_topk(xd.data_ptr(), xd.stride(0), wd.data_ptr(), bd.data_ptr(), T, H, E, topk,
+                                  ids.data_ptr(), w.data_ptr(), logits.data_ptr(), None, stream(xd.device)), "router")
+    torch.cuda.synchronize()
+    rid, rw, rl = O.router(bits(x), bits(wr), bias.numpy(), topk)
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), np.asarray(rl, dtype=np.float32).view(np.uint32))
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("T", [1, 6, 12, 150])
 def test_router_ties_to_lower_id(T):
     """Duplicated router rows give exactly equal logits: the lower expert id is selected first."""
     H, E, topk = 2048, 512, 10
