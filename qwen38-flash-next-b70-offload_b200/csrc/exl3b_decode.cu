@@ -387,7 +387,7 @@ __device__ __forceinline__ void group_small(const DecodeArgs& a, SmallTab& tb) {
 
 // Cached calls run the device cache step first (in place on ids / w), then the grouping.  Small batches try the
 // one-warp path first (the other warps zero the arrival counters meanwhile).
-__global__ void __launch_bounds__(1024) prep_kernel(EnsureArgs ea, DecodeArgs da, int cached) {
+__global__ void __launch_bounds__(1024, 1) prep_kernel(EnsureArgs ea, DecodeArgs da, int cached) {   // 64 registers: no spills
     __shared__ int sh_fast;
     pdl_wait();
     pdl_trigger();
