@@ -33,7 +33,7 @@ BLOB = 1786368
 PF_T = 8192          # configs[2] prefill chunk
 # DRAM bytes (read + write) of one decode gate-up launch at batch 1, from one ncu capture of gu_cluster_kernel<3> on
 # the same per-layer work (4-layer stack): dram__bytes_read.sum + dram__bytes_write.sum
-GU_TRAFFIC_BS1 = 12013312
+GU_TRAFFIC_BS1 = 11997696
 PF_KEY0 = 1 << 20    # blob keys of the prefill layer (distinct from the decode stack's)
 # router weight std: x . Wr then has the std of a standard Gumbel variable (pi / sqrt(6) = 1.28), so -1.1 ln(rank) +
 # router noise makes each layer's top-10 a Zipf(1.1)-like Plackett-Luce sample and picks miss the 8,000-slot cache
