@@ -55,6 +55,7 @@ struct DecodeArgs {
 };
 
 constexpr int kSmallPicks = 32;   // small-batch mode: up to 32 picks (3 tokens at top-10)
+static_assert(kSmallPicks <= kDeferMaskMax, "the cache step defers the tier-mask rewrite of every small batch");
 
 // Grouping of a small batch in shared memory (the entry tables of route_prep_block, plus per-pick flags).
 struct SmallTab {
@@ -218,14 +219,20 @@ __device__ __forceinline__ bool prep_fast_warp(const EnsureArgs& ea, const Decod
     if (cached) {
         const long long pt_safe = tier ? (long long)a.ptrs[safe] : 0;
         const int kv_safe = (tier && a.kinfo) ? a.kinfo[safe] : kpack;
-        // 1. tier mask in ascending pick index: ring log, pick -> (safe, 0)
+        // 1. tier mask in ascending pick index: ring log, pick -> (safe, 0).  Of a call's masked picks only the last
+        // ring_cap land in the ring (sequentially, earlier ones would be overwritten within the call): each slot is
+        // written once, so parallel writes give the sequential result.
+        int nmask = 0;
+#pragma unroll
+        for (int j = 0; j < J; ++j) nmask += __popc(__ballot_sync(FULL, masked[j]));
         int base = ring0;
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const unsigned bm = __ballot_sync(FULL, masked[j]);
             if (masked[j]) {
                 const int i = lane + 32 * j;
-                ea.ring[1 + ((base + __popc(bm & lt)) % ea.ring_cap)] = L * E + id[j];
+                const int c = base - ring0 + __popc(bm & lt);   // rank among the call's masked picks
+                if (c >= nmask - ea.ring_cap) ea.ring[1 + ((base + __popc(bm & lt)) % ea.ring_cap)] = L * E + id[j];
                 if (!ea.defer_mask) {   // deferred: the last down block rewrites ids / w
                     ea.ids[i] = safe;
                     ea.w[i] = 0.0f;

@@ -12,6 +12,7 @@
 namespace exl3b {
 
 constexpr int kEnsureThreads = 1024;
+constexpr int kDeferMaskMax = 64;   // most picks of a call whose tier-mask rewrite may be deferred
 
 // Block-wide exclusive scan of one int per thread (1024 threads); returns the prefix, *total gets the sum.
 __device__ __forceinline__ int block_scan(int v, int* total, int* sh_warp /* [32] */) {
@@ -46,7 +47,7 @@ struct EnsureArgs {
     const int64_t* host_base; int64_t slot_base; int64_t blob; int64_t hstride;
     int64_t* fill_all; int32_t* fill_list; int max_fill; int prefetch; int32_t* pf_slot;
     const uint8_t* ram_res; int32_t* ring; int ring_cap; const int32_t* safe; int32_t* vict;
-    int defer_mask = 0;   // 1: the masked picks' in-place (safe, 0) rewrite of ids / w is left to the caller's last
+    int defer_mask = 0;   // 1 (npairs <= kDeferMaskMax): the masked picks' in-place (safe, 0) rewrite of ids / w is left to the caller's last
                           // kernel (npairs <= 32); the step itself uses the masked ids
 };
 
@@ -57,17 +58,31 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     __shared__ int miss[1024];
     __shared__ int vslot[1024];
     __shared__ int hist[256];
-    __shared__ unsigned char s_msk[32];   // defer_mask: picks masked by step 1
+    __shared__ unsigned char s_msk[kDeferMaskMax];   // defer_mask: picks masked by step 1
     const int tid = threadIdx.x;
     const int E = a.E, S = a.S, L = a.layer;
     int total;
 
     // 1. tier mask, picks in ascending index
     if (a.defer_mask)
-        for (int i = tid; i < 32; i += kEnsureThreads) s_msk[i] = 0;
+        for (int i = tid; i < kDeferMaskMax; i += kEnsureThreads) s_msk[i] = 0;
     if (a.ram_res && !a.prefetch) {
+        // the call's masked-pick count first: only the last ring_cap of them land in the ring (sequentially, earlier
+        // ones would be overwritten within the call), so every slot is written once and parallel writes give the
+        // sequential result
+        int nmask = 0;
+        for (int c0 = 0; c0 < a.npairs; c0 += kEnsureThreads) {
+            int i = c0 + tid, flag = 0;
+            if (i < a.npairs) {
+                const int key = L * E + a.ids[i];
+                flag = (a.slot_of[key] < 0 && !a.ram_res[key]) ? 1 : 0;
+            }
+            block_scan(flag, &total, sh_warp);
+            nmask += total;
+        }
         if (tid == 0) sh_base_ring = a.ring[0];
         __syncthreads();
+        const int ring0 = sh_base_ring;
         for (int c0 = 0; c0 < a.npairs; c0 += kEnsureThreads) {
             int i = c0 + tid;
             int flag = 0, key = 0;
@@ -78,7 +93,7 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
             int pre = block_scan(flag, &total, sh_warp);
             if (flag) {
                 int c = sh_base_ring + pre;
-                a.ring[1 + (c % a.ring_cap)] = key;
+                if (c - ring0 >= nmask - a.ring_cap) a.ring[1 + (c % a.ring_cap)] = key;
                 if (a.defer_mask) {
                     s_msk[i] = 1;
                 } else {

@@ -148,6 +148,17 @@ def test_decode_layer_small(T):
     check_decode(x, ids, w, ptrs, views, H, I, K, E)
 
 
+@pytest.mark.parametrize("T", [4, 6, 7])
+def test_decode_layer_top10_shared_experts(T):
+    """Top-10 of 16 experts: 40 / 60 picks go through the small-batch grouping (two picks per lane, most experts
+    shared by several tokens), 70 through the grouped path."""
+    H, I, E, topk, K = 256, 128, 16, 10, 3
+    blobs, ptrs, views = make_layer(E, H, I, K, seed=23)
+    x = synth.activations(T, H, 40 + T)
+    ids, w = _route(T, E, topk, 60 + T)
+    check_decode(x, ids, w, ptrs, views, H, I, K, E)
+
+
 @pytest.mark.parametrize("T", [1, 4])
 def test_decode_layer_full_shape(T):
     """Config 1 (T=1) and the bs-4 decode shape: H=2048, I=768, 512 experts, top-10, K=3, router in the loop."""
@@ -300,8 +311,9 @@ def test_forward_cached_matches_forward_and_oracle_state():
             assert torch.equal(st.slots[s].cpu(), st.host[keys[li]][e])
 
 
-def test_tier_mask_ring_and_safe():
-    H, I, K, E, S, L, topk = 256, 128, 3, 16, 6, 2, 4
+@pytest.mark.parametrize("T,topk", [(2, 4), (6, 10)])
+def test_tier_mask_ring_and_safe(T, topk):
+    H, I, K, E, S, L = 256, 128, 3, 16, 6, 2
     st = _store(H, I, K, E, S, L, seed=17)
     keys = list(st.layer_index)
     ram_res = torch.zeros(L * E, dtype=torch.uint8, device=DEV)
@@ -315,8 +327,8 @@ def test_tier_mask_ring_and_safe():
         sf = safe.cpu().numpy()
         for step in range(6):
             li = step % L
-            x = synth.activations(2, H, 400 + step).to(DEV)
-            ids, w = _route(2, E, topk, 500 + step)
+            x = synth.activations(T, H, 400 + step).to(DEV)
+            ids, w = _route(T, E, topk, 500 + step)
             idd, wd = ids.to(DEV), w.to(DEV)
             y = st.forward_cached(keys[li], x, idd, wd)
             ni, nw = ids.numpy().copy(), w.numpy().copy()
