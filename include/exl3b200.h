@@ -116,7 +116,7 @@ int exl3b_align(const int32_t* ids, const float* w, int P, int topk, int E, int 
 
 /* No counterpart in the reference.  exl3b_moe_decode for callers that cannot allocate device memory: the same
  * kernels and arguments without workspace / ws_bytes; the scratch is a fixed 8 MiB device array of the library
- * (exl3b_moe_decode_workspace(M, topk, H, I) must be <= 8 MiB: up to 5 tokens at top-10 with H = 2048, I = 768; larger
+ * (exl3b_moe_decode_workspace(M, topk, H, I) must be <= 8 MiB: up to 85 tokens at top-10 with H = 2048, I = 768; larger
  * calls return EXL3B_EINVAL).  The first call on each device looks the array's address up, so make it before any
  * stream capture on that device.  Nothing has to be zeroed by the caller.  One scratch per device: calls that overlap
  * on one device race; order them on one stream or with events. */

@@ -1,23 +1,26 @@
 // exl3b_decode.cu -- routed-MoE decode path (few tokens): the reference's launch_ensure + GateUpKernel + DownKernel +
 // CombineKernel (exl3_moe.a8.sycl:121-395, 837-1040, 1229-1314) re-designed for sm_100a.
 //
-// Three kernels per call, chained with programmatic dependent launch:
+// Three kernels per call (after the router), chained with programmatic dependent launch:
 //   prep    (1 block): [device cache step: tier mask, LRU stamps, victims, fill plan] + grouping of the active picks
 //                      by DISTINCT expert into entries (one expert, up to 8 of its picks), so an expert picked by several
 //                      tokens is streamed once;
-//   gate-up (grid)   : copies the planned cache fills (host blob -> slot) and runs units (entry, projection, 128-column
-//                      block, 128-row k block);
-//   down    (grid)   : units (entry, 128-column block of H, 128-row k block of I), the weighted combine, and the cache
-//                      commit (ptrs[e] = slot) by the last block to finish.
+//   gate-up (clusters of 4 CTAs per (entry, 128-column block of I)): each CTA streams split-K units (projection,
+//                      128-row k block) of one projection; the CTAs' sums meet in rank 0's shared memory (DSMEM), which
+//                      runs the epilogue; then the CTAs copy the planned cache fills (host blob -> slot);
+//   down    (one CTA per (entry, 128-column block of H)): the item's strip rows split evenly over the 8 warps, a
+//                      shared-memory reduction, the epilogue and the weighted combine, and the cache commit
+//                      (ptrs[e] = slot) by the last block to arrive.
+// Small batches (<= 32 picks) skip the wait for prep: gate-up and down group the picks themselves (group_small) and the
+// tier mask's rewrite of ids / w is written by the last down block.
 // Each warp streams its units' 8-tile strips through a private SMEM ring filled by cp.async, decodes each lane's 8
 // values of a tile straight into an mma.sync A fragment of W^T (exl3b_common.cuh) and multiplies it with the 8-token
-// Hadamard-domain activation block (fp32 accumulate).  Split-K partials go to a small L2-resident buffer; the last
-// warp to finish a column block (atomic arrival counter, no waiting) reduces them in fixed order and runs the
-// epilogue, so results do not depend on scheduling:
+// Hadamard-domain activation block (fp32 accumulate).  Every reduction runs in a fixed order (warp order, cluster
+// rank order, pick order), so results do not depend on scheduling:
 //   gate/up epilogue (:239-256): g = fp16(FWHT(g) r svh_g), u likewise, a = fp16(SiLU(g) u), a = fp16(a suh_d),
 //                                abuf = fp16(FWHT(a) r)
 //   down epilogue   (:355-364): y = FWHT(v) (r w) svh_d (fp32)
-//   combine         (:387-394): out[m] = sum_k y[m,k] in fixed k order, by the last column block to finish.
+//   combine         (:387-394): out[m] = sum_k y[m,k] in fixed k order, by the last of the token's picks to finish.
 // Cache fills are read from their host address (ptrs[e] until the commit), like the reference's write-through, while
 // the gate-up blocks copy them into their slots.  Picks with weight exactly 0 (tier-masked) contribute exactly zero
 // and are skipped (flag bit 0).
@@ -44,8 +47,8 @@ struct DecodeArgs {
     int* ent_expert; int* ent_n; int* ent_tok; float* ent_w; int* ent_pick; int* n_ent;
     long long* ent_blob; int* ent_k;
     int* tok_cnt; int* pick_act;
-    int* cnt_gu; int* cnt_d; int* cnt_c; int* blocks_done;
-    __half* abuf; float* part_gu; float* part_d; float* y;
+    int* cnt_c; int* blocks_done;
+    __half* abuf; float* y;
     int maxent;
     // small batches (M <= kTokPerEnt, M topk <= kSmallPicks): the gate-up and down kernels group the picks themselves
     // from ids / w and the layer's tier state (t_*: null without a cache or tier); the tier mask's in-place rewrite
@@ -83,9 +86,7 @@ __device__ __forceinline__ void route_prep_block(const DecodeArgs& a) {
     __shared__ int s_ids[kPrepChunk];
     __shared__ float s_w[kPrepChunk];
     const int tid = threadIdx.x, npairs = a.M * a.topk;
-    const int nbI = a.I / 128, nbH = a.H / 128;
-    for (int i = tid; i < a.maxent * nbI; i += blockDim.x) a.cnt_gu[i] = 0;
-    for (int i = tid; i < a.maxent * nbH; i += blockDim.x) a.cnt_d[i] = 0;
+    const int nbH = a.H / 128;
     for (int i = tid; i < a.M * nbH; i += blockDim.x) a.cnt_c[i] = 0;
     if (tid == 0) a.blocks_done[0] = 0;
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
@@ -403,9 +404,7 @@ __global__ void __launch_bounds__(1024, 1) prep_kernel(EnsureArgs ea, DecodeArgs
             const bool ok = prep_fast_warp(ea, da, cached);
             if (threadIdx.x == 0) sh_fast = ok ? 1 : 0;
         } else {
-            const int nbI = da.I / 128, nbH = da.H / 128;
-            for (int i = threadIdx.x - 32; i < da.maxent * nbI; i += blockDim.x - 32) da.cnt_gu[i] = 0;
-            for (int i = threadIdx.x - 32; i < da.maxent * nbH; i += blockDim.x - 32) da.cnt_d[i] = 0;
+            const int nbH = da.H / 128;
             for (int i = threadIdx.x - 32; i < da.M * nbH; i += blockDim.x - 32) da.cnt_c[i] = 0;
             if (threadIdx.x == 32) da.blocks_done[0] = 0;
         }
@@ -1107,8 +1106,13 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------ host
+// Decode workspace: the entry tables (prep's grouping), per-token / per-pick flags and counters, the activation
+// rows between the kernels (abuf: fp16 [pick][I]) and the weighted pick outputs (y: fp32 [pick][H]), 256-byte
+// aligned pieces.
+enum WsPart { kWsEntExpert, kWsEntN, kWsEntTok, kWsEntW, kWsEntPick, kWsNEnt, kWsTokCnt, kWsPickAct, kWsCntC, kWsAbuf,
+              kWsY, kWsEntBlob, kWsEntK, kWsBlocksDone, kWsParts };
 struct WsLayout {
-    size_t off[18];
+    size_t off[kWsParts];
     size_t total;
 };
 
@@ -1122,13 +1126,25 @@ void prof_record(int i, cudaStream_t s) {
 }
 
 static WsLayout ws_layout(int M, int topk, int H, int I) {
-    size_t np = (size_t)M * topk, me = np, nbI = I / 128, nbH = H / 128, nKB = H / 128, nKBd = I / 128;
-    size_t sizes[18] = {me * 4, me * 4, me * kTokPerEnt * 4, me * kTokPerEnt * 4, me * kTokPerEnt * 4, 16,
-                        (size_t)M * 4, np * 4, me * nbI * 4, me * nbH * 4, (size_t)M * nbH * 4,
-                        np * I * 2, np * 2 * nKB * I * 4, np * nKBd * H * 4, np * H * 4, me * 8, me * 4, 16};
+    const size_t np = (size_t)M * topk, me = np, nbH = H / 128;
+    size_t sizes[kWsParts];
+    sizes[kWsEntExpert] = me * 4;
+    sizes[kWsEntN] = me * 4;
+    sizes[kWsEntTok] = me * kTokPerEnt * 4;
+    sizes[kWsEntW] = me * kTokPerEnt * 4;
+    sizes[kWsEntPick] = me * kTokPerEnt * 4;
+    sizes[kWsNEnt] = 16;
+    sizes[kWsTokCnt] = (size_t)M * 4;
+    sizes[kWsPickAct] = np * 4;
+    sizes[kWsCntC] = (size_t)M * nbH * 4;
+    sizes[kWsAbuf] = np * I * 2;
+    sizes[kWsY] = np * H * 4;
+    sizes[kWsEntBlob] = me * 8;
+    sizes[kWsEntK] = me * 4;
+    sizes[kWsBlocksDone] = 16;
     WsLayout L;
     size_t o = 0;
-    for (int i = 0; i < 18; ++i) { L.off[i] = o; o += al256(sizes[i]); }
+    for (int i = 0; i < kWsParts; ++i) { L.off[i] = o; o += al256(sizes[i]); }
     L.total = o;
     return L;
 }
@@ -1208,13 +1224,13 @@ static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int6
     EXL3B_CHECK(workspace && ws_bytes >= (int64_t)L.total, "exl3b_moe_decode: workspace too small");
     EXL3B_CHECK((((uintptr_t)workspace) & 255) == 0, "exl3b_moe_decode: workspace must be 256-byte aligned");
     char* b = (char*)workspace;
-    a.ent_expert = (int*)(b + L.off[0]); a.ent_n = (int*)(b + L.off[1]); a.ent_tok = (int*)(b + L.off[2]);
-    a.ent_w = (float*)(b + L.off[3]); a.ent_pick = (int*)(b + L.off[4]); a.n_ent = (int*)(b + L.off[5]);
-    a.tok_cnt = (int*)(b + L.off[6]); a.pick_act = (int*)(b + L.off[7]);
-    a.cnt_gu = (int*)(b + L.off[8]); a.cnt_d = (int*)(b + L.off[9]); a.cnt_c = (int*)(b + L.off[10]);
-    a.abuf = (__half*)(b + L.off[11]); a.part_gu = (float*)(b + L.off[12]); a.part_d = (float*)(b + L.off[13]);
-    a.y = (float*)(b + L.off[14]);
-    a.ent_blob = (long long*)(b + L.off[15]); a.ent_k = (int*)(b + L.off[16]); a.blocks_done = (int*)(b + L.off[17]);
+    a.ent_expert = (int*)(b + L.off[kWsEntExpert]); a.ent_n = (int*)(b + L.off[kWsEntN]);
+    a.ent_tok = (int*)(b + L.off[kWsEntTok]); a.ent_w = (float*)(b + L.off[kWsEntW]);
+    a.ent_pick = (int*)(b + L.off[kWsEntPick]); a.n_ent = (int*)(b + L.off[kWsNEnt]);
+    a.tok_cnt = (int*)(b + L.off[kWsTokCnt]); a.pick_act = (int*)(b + L.off[kWsPickAct]);
+    a.cnt_c = (int*)(b + L.off[kWsCntC]); a.abuf = (__half*)(b + L.off[kWsAbuf]); a.y = (float*)(b + L.off[kWsY]);
+    a.ent_blob = (long long*)(b + L.off[kWsEntBlob]); a.ent_k = (int*)(b + L.off[kWsEntK]);
+    a.blocks_done = (int*)(b + L.off[kWsBlocksDone]);
     a.maxent = M * topk;
     a.small = (M <= kTokPerEnt && M * topk <= kSmallPicks && !(ea && ea->prefetch)) ? 1 : 0;
     EnsureArgs none{};

@@ -4,7 +4,7 @@
 //
 // Limits:
 //   * kNoallocScratchBytes = 8 MiB per device: exl3b_moe_decode_workspace(M, topk, H, I) must fit, which covers up to
-//     5 tokens at top-10 with H = 2048, I = 768 (1.5 MiB per token there).  Larger calls are rejected with
+//     85 tokens at top-10 with H = 2048, I = 768 (about 94 KiB per token there).  Larger calls are rejected with
 //     EXL3B_EINVAL before anything is launched.
 //   * Set-up: the first call on each device looks the array's device address up (cudaGetSymbolAddress, with that
 //     device current) and keeps it; make that first call before any stream capture on the device.

@@ -33,9 +33,9 @@ def _decode_noalloc(L, x, ids, w, ptrs, I, K, E, out):
 
 
 def test_noalloc_rejects_oversized_call():
-    """9 tokens at top-10, H=2048, I=768 need 13.5 MiB of scratch: rejected before any launch (no GPU needed)."""
+    """100 tokens at top-10, H=2048, I=768 need 9.4 MiB of scratch: rejected before any launch (no GPU needed)."""
     L = _lib.lib()
-    rc = L.exl3b_moe_decode_noalloc(1 << 20, 2048, 1, 1 << 20, 1 << 20, 9, 10, 1 << 20, None, 2048, 768, 3, 512,
+    rc = L.exl3b_moe_decode_noalloc(1 << 20, 2048, 1, 1 << 20, 1 << 20, 100, 10, 1 << 20, None, 2048, 768, 3, 512,
                                     1 << 20, 2048, 1, 0, None)
     assert rc == 1
     assert b"8 MiB" in ctypes.string_at(L.exl3b_last_error())
