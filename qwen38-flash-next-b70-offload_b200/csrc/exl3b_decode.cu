@@ -724,13 +724,23 @@ __device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, 
     const int tcnt = tb ? (int)tb->tok_cnt[mt] : __ldcg(a.tok_cnt + mt);
     if (oc == tcnt - 1) {
         __threadfence();
+        // up to 12 picks' rows and flags loaded at once (one round trip), then summed in pick order; rows of
+        // inactive picks (in bounds, never written this call) are loaded and skipped
+        constexpr int kComb = 12;
         float sm[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int k = 0; k < a.topk; ++k) {
-            int pp = mt * a.topk + k;
-            if (!(tb ? (int)tb->act[pp] : __ldcg(a.pick_act + pp))) continue;
-            float4 q4 = __ldcg(reinterpret_cast<const float4*>(a.y + (size_t)pp * a.H + nbh * 128 + 4 * lane));
-            sm[0] += q4.x; sm[1] += q4.y; sm[2] += q4.z; sm[3] += q4.w;
+        for (int k0 = 0; k0 < a.topk; k0 += kComb) {
+            float4 q4[kComb];
+            int on[kComb];
+#pragma unroll
+            for (int j = 0; j < kComb; ++j) {
+                const int k = k0 + j, pp = mt * a.topk + k;
+                on[j] = k < a.topk ? (tb ? (int)tb->act[pp] : __ldcg(a.pick_act + pp)) : 0;
+                q4[j] = k < a.topk ? __ldcg(reinterpret_cast<const float4*>(a.y + (size_t)pp * a.H + nbh * 128 + 4 * lane))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < kComb; ++j)
+                if (on[j]) { sm[0] += q4[j].x; sm[1] += q4[j].y; sm[2] += q4[j].z; sm[3] += q4[j].w; }
         }
         store_out(a, (long long)mt * a.os + nbh * 128 + 4 * lane, sm);
     }
