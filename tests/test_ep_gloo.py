@@ -1,5 +1,5 @@
-"""CPU, world_size 2 (gloo): the expert-parallel prefill exchange (exl3b200.ep.EPPrefill) with host stand-ins for
-the device steps.  Every rank's output equals the one-device prefill of its tokens (oracle, same picks) within the
+"""CPU, world_size 2 and 4 (gloo): the expert-parallel prefill exchange (exl3b200.ep.EPPrefill) with host stand-ins
+for the device steps.  Every rank's output equals the one-device prefill of its tokens (oracle, same picks) within the
 layer tolerance; a rank with no tokens and a rank whose tokens all stay local are covered."""
 import os
 import socket
@@ -62,14 +62,14 @@ def _worker(rank, world, port, case, q):
         dist.destroy_process_group()
 
 
-def _run(case):
+def _run(case, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
     for p in ps:
         p.start()
-    res = [q.get(timeout=240) for _ in range(2)]
+    res = [q.get(timeout=240) for _ in range(world)]
     for p in ps:
         p.join(timeout=60)
     for rank, status, _ in res:
@@ -89,3 +89,13 @@ def test_ep_rank_without_tokens():
 def test_ep_tokens_all_local():
     last = _run({"T": [5, 4], "local_only": True})
     assert last[0]["send_counts"][1] == 0
+
+
+def test_ep_exchange_four_ranks():
+    """Four ranks (two experts each), one of them without tokens: every rank sends to and receives from the others
+    in rank order."""
+    last = _run({"T": [5, 0, 7, 3]}, world=4)
+    assert last[1]["send_rows"] == 0
+    assert sum(last[r]["recv_rows"] for r in range(4)) == sum(last[r]["send_rows"] for r in range(4))
+    for r in range(4):
+        assert [last[d]["recv_counts"][r] for d in range(4)] == last[r]["send_counts"]
