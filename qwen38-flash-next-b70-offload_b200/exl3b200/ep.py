@@ -90,7 +90,13 @@ class EPPrefill:
         self.last = {}
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits):
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        # A peer that stopped (exited, or stuck past the group's timeout) fails the collective; the error names the
+        # layer step so that the caller can tell a lost rank from a bad argument.
+        try:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        except RuntimeError as e:   # torch's distributed backend errors derive from RuntimeError
+            raise RuntimeError(f"exl3b200 EPPrefill: all-to-all failed on rank {self.rank} of {self.G} "
+                               f"(a peer rank stopped or timed out): {e}") from e
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         G, H = self.G, self.H

@@ -99,3 +99,60 @@ def test_ep_exchange_four_ranks():
     assert sum(last[r]["recv_rows"] for r in range(4)) == sum(last[r]["send_rows"] for r in range(4))
     for r in range(4):
         assert [last[d]["recv_counts"][r] for d in range(4)] == last[r]["send_counts"]
+
+
+def _fail_worker(rank, world, port, q):
+    """Rank 1 leaves right after joining the group (no collective); rank 0 runs a layer and must get an error."""
+    import sys
+    sys.path[:0] = [os.path.join(ROOT, "qwen38-flash-next-b70-offload_b200"), os.path.join(ROOT, "oracle"),
+                    os.path.join(ROOT, "tests")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    def report(msg):   # flush the queue's feeder thread before the hard exit
+        q.put((rank, msg))
+        q.close()
+        q.join_thread()
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        report("left")
+        os._exit(0)
+    try:
+        from ep_host import HostEPKernels
+        from exl3b200 import synth
+        from exl3b200.ep import EPPrefill
+        E, H, I, K, topk, T = 8, 256, 128, 3, 3, 4
+        blobs = [synth.make_blob(11, e, H, I, K).numpy() for e in range(E)]
+        g = torch.Generator().manual_seed(5)
+        ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).to(torch.int32)
+        w = torch.full((T, topk), 1.0 / topk)
+        x = synth.activations(T, H, 9)
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, torch.zeros(E // world, dtype=torch.int64),
+                       kernels=HostEPKernels(blobs[:E // world], H, I, K))
+        ep.forward(x, ids, w)
+        report("no error")
+    except RuntimeError as e:
+        report("raised: " + str(e)[:300])
+    except Exception as e:
+        report(f"other {type(e).__name__}: {e}")
+    os._exit(0)   # no teardown against the departed peer
+
+
+def test_ep_peer_failure_raises():
+    """A rank that stops ends the other rank's next layer with a RuntimeError naming the exchange (bounded by the
+    group's 10 s timeout), not a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_fail_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("raised:") and "EPPrefill" in res[0], res[0]
