@@ -1,0 +1,157 @@
+"""CPU: exl3b200.tier.TierHost, the per-step host loop of the RAM tier, against fakes of the device state.
+
+The device side is plain CPU tensors written the way the decode kernels write them: masked picks log their keys to
+the miss ring (ring[0] counts, key n at ring[1 + n % cap]), the victim write-back sets ram_res[key].  The host loop
+consumes each snapshot one step later, so a key logged before step t is fetched by step t + 1.
+"""
+import numpy as np
+import torch
+
+from exl3b200.tier import TierHost
+
+
+class FakeDevice:
+    def __init__(self, n_keys=16, cap=8):
+        self.ram_res = torch.zeros(n_keys, dtype=torch.uint8)
+        self.ring = torch.zeros(1 + cap, dtype=torch.int32)
+        self.slot_of = torch.full((n_keys,), -1, dtype=torch.int32)
+        self.cap = cap
+
+    def log_misses(self, keys):   # what a decode step does for its masked picks
+        for key in keys:
+            n = int(self.ring[0])
+            self.ring[1 + n % self.cap] = key
+            self.ring[0] = n + 1
+
+    def victim_writeback(self, key):
+        self.ram_res[key] = 1
+
+
+def _tier(dev, **kw):
+    fetched, released = [], []
+    kw.setdefault("budget", 8)
+    t = TierHost(dev.ram_res, dev.ring, dev.slot_of, fetch=fetched.append, release=released.append, **kw)
+    return t, fetched, released
+
+
+def test_misses_are_fetched_then_flagged():
+    dev = FakeDevice()
+    t, fetched, _ = _tier(dev)
+    assert t.step() == 0                    # first snapshot: nothing to consume
+    dev.log_misses([3, 5, 3])
+    t.step()                                # consumes the snapshot taken before the misses
+    assert fetched == []
+    assert t.step() == 3
+    assert fetched == [3, 5]                # most-logged first
+    t.fill_done(3)
+    t.fill_done(5)
+    t.step()
+    assert dev.ram_res[3] == 1 and dev.ram_res[5] == 1 and t.resident() == 2
+    dev.log_misses([3])                     # resident or already fetched: not fetched again
+    t.step()
+    t.step()
+    assert fetched == [3, 5]
+
+
+def test_budget_drops_vram_copies_first_then_oldest():
+    dev = FakeDevice()
+    t, fetched, released = _tier(dev, budget=3)
+    t.step()
+    for key in [1, 2, 4]:                   # resident at steps 2, 3, 4
+        dev.log_misses([key])
+        t.step()
+        t.step()
+        t.fill_done(key)
+    t.step()
+    assert sorted(np.nonzero(t.res)[0].tolist()) == [1, 2, 4]
+    dev.slot_of[4] = 0                      # key 4 also sits in VRAM now
+    dev.log_misses([7, 9])                  # two wanted keys need two places
+    t.step()
+    t.step()
+    assert fetched[-2:] == [7, 9]
+    assert t.res[4] == 0 and t.res[1] == 0 and t.res[2] == 1   # the VRAM copy, then the oldest
+    assert dev.ram_res[4] == 0 and dev.ram_res[1] == 0
+    assert released == []                   # released only after the device ran a step past the clear
+    t.step()
+    t.step()
+    assert sorted(released) == [1, 4]
+
+
+def test_victim_writeback_becomes_resident_and_rescues_a_drop():
+    dev = FakeDevice()
+    t, fetched, released = _tier(dev, budget=2)
+    t.step()
+    dev.victim_writeback(6)                 # the kernel copied an evicted VRAM expert to its host slot
+    t.step()
+    dev.victim_writeback(5)
+    t.step()
+    t.step()
+    assert t.res[6] == 1 and t.res[5] == 1 and t.stats["victims_kept"] == 2
+    dev.log_misses([2])                     # over budget: the oldest (6) is dropped for 2
+    t.step()
+    t.step()
+    assert t.res[6] == 0 and t.res[5] == 1 and fetched == [2]
+    dev.victim_writeback(6)                 # the next step wrote 6 back before its host copy was released
+    t.step()
+    t.step()
+    assert 6 not in released and t.stats["release_rescued"] == 1
+    assert t.res[6] == 1 and t.res[5] == 0  # 6 is resident again (youngest); 5 made room
+
+
+def test_pinned_keys_are_never_dropped():
+    dev = FakeDevice()
+    pinned = np.zeros(16, dtype=bool)
+    pinned[0] = True
+    dev.ram_res[0] = 1
+    t, fetched, released = _tier(dev, budget=1, pinned=pinned)
+    t.step()
+    dev.log_misses([5])
+    t.step()
+    t.step()
+    assert t.res[0] == 1 and fetched == [] and t.stats["admit_deferred"] == 1
+
+
+def test_ring_overflow_keeps_the_last_cap_keys():
+    dev = FakeDevice(cap=8)
+    t, fetched, _ = _tier(dev, budget=16)
+    t.step()
+    dev.log_misses(list(range(12)))         # 12 keys through an 8-entry ring: 0-3 were overwritten
+    t.step()
+    assert t.step() == 8
+    assert t.stats["ring_overflow"] == 4
+    assert sorted(fetched) == list(range(4, 12))
+
+
+def test_admission_limits_keys_in_flight():
+    dev = FakeDevice()
+    t, fetched, _ = _tier(dev, budget=16, max_inflight=2)
+    t.step()
+    dev.log_misses([9, 8, 8, 7, 7, 7])
+    t.step()
+    t.step()
+    assert fetched == [7, 8] and t.stats["admit_deferred"] == 1   # most-logged first; 9 stays masked
+    t.fill_done(7)
+    t.fill_done(8)
+    dev.log_misses([9])                     # re-logged on its next miss
+    t.step()
+    t.step()
+    assert fetched == [7, 8, 9]
+
+
+def test_min_age_protects_fresh_fills():
+    dev = FakeDevice()
+    t, fetched, _ = _tier(dev, budget=1, min_age=3)
+    t.step()
+    dev.log_misses([1])
+    t.step()
+    t.step()
+    t.fill_done(1)
+    t.step()                                # 1 resident at this step
+    dev.log_misses([2])
+    t.step()
+    t.step()                                # 1 is younger than 3 steps: 2 waits
+    assert t.res[1] == 1 and fetched == [1]
+    for _ in range(3):
+        dev.log_misses([2])
+        t.step()
+    assert fetched == [1, 2] and t.res[1] == 0
