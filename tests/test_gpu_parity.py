@@ -311,6 +311,28 @@ def test_forward_cached_matches_forward_and_oracle_state():
             assert torch.equal(st.slots[s].cpu(), st.host[keys[li]][e])
 
 
+def test_forward_prefill_staged_matches_host_pointers():
+    """Staged prefill (moe_offload.py:348-437): each layer's non-resident experts are copied to a device staging
+    buffer on a side stream, double-buffered across layers; the outputs equal the same layers read through host
+    pointers, bitwise, over two passes of the layers."""
+    H, I, K, E, S, L, topk, T = 256, 128, 3, 32, 12, 3, 4, 300
+    st = _store(H, I, K, E, S, L, seed=29)
+    keys = list(st.layer_index)
+    for li, key in enumerate(keys):
+        st.make_resident(key, list(range(li, E, 8)))   # four experts per layer in VRAM, the rest staged
+    torch.cuda.synchronize()
+    gold = {k: torch.tensor(st._host_ptr[k].tolist(), dtype=torch.int64, device=DEV) for k in keys}
+    for rep in range(2):
+        for li, key in enumerate(keys):
+            x = synth.activations(T, H, 900 + 10 * rep + li).to(DEV)
+            ids, w = _route(T, E, topk, 950 + 10 * rep + li)
+            idd, wd = ids.to(DEV), w.to(DEV)
+            y = st.forward_prefill_staged(key, x, idd, wd)
+            yr = st.forward(key, x, idd, wd, ptrs=gold[key])
+            torch.cuda.synchronize()
+            assert torch.equal(y, yr), (rep, li)
+
+
 @pytest.mark.parametrize("T,topk", [(2, 4), (6, 10)])
 def test_tier_mask_ring_and_safe(T, topk):
     H, I, K, E, S, L = 256, 128, 3, 16, 6, 2
