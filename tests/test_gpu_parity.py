@@ -368,6 +368,47 @@ def test_tier_mask_ring_and_safe(T, topk):
                        torch.zeros(0, dtype=torch.int32))
 
 
+def test_tier_host_loop_admits_missed_experts():
+    """The RAM tier's host loop (exl3b200.tier.TierHost) against the decode kernels: picks in neither VRAM nor RAM
+    are masked and logged; the loop fetches them (host copies are always valid here, so fetch completes at once) and
+    uploads their flags; the next call reads them unmasked, bitwise equal to the all-host-pointer layer."""
+    from exl3b200.tier import TierHost
+    H, I, K, E, S, L = 256, 128, 3, 16, 4, 1
+    st = _store(H, I, K, E, S, L, seed=31)
+    key = list(st.layer_index)[0]
+    gold = torch.tensor(st._host_ptr[key].tolist(), dtype=torch.int64, device=DEV)
+    ram_res = torch.zeros(L * E, dtype=torch.uint8, device=DEV)
+    ram_res[0] = 1                             # the safe expert
+    ring = torch.zeros(1 + 16, dtype=torch.int32, device=DEV)
+    safe = torch.zeros(L, dtype=torch.int32, device=DEV)
+    pinned = np.zeros(L * E, dtype=bool)
+    pinned[0] = True
+    X.moe_set_tier(ram_res, ring, safe)
+    try:
+        tier = TierHost(ram_res, ring, st.slot_of_dev, budget=L * E, fetch=lambda k: tier.fill_done(k),
+                        pinned=pinned)
+        ids = torch.tensor([[5, 6, 7, 8], [9, 10, 11, 12]], dtype=torch.int32)
+        w = torch.full((2, 4), 0.25)
+        x = synth.activations(2, H, 77).to(DEV)
+        idd, wd = ids.to(DEV), w.to(DEV)
+        st.forward_cached(key, x, idd, wd)     # every pick masked (VRAM and RAM hold none of them) and logged
+        torch.cuda.synchronize()
+        assert torch.all(wd == 0) and int(ring[0]) == 8
+        for _ in range(3):                     # snapshot, fetch, flag upload
+            tier.step()
+        torch.cuda.synchronize()
+        assert ram_res[5:13].cpu().tolist() == [1] * 8 and tier.stats["fetches"] == 8
+        idd, wd = ids.to(DEV), w.to(DEV)
+        y = st.forward_cached(key, x, idd, wd)
+        yr = exops.moe_decode(x, ids.to(DEV), w.to(DEV), gold, I, K, E)
+        torch.cuda.synchronize()
+        assert torch.equal(idd.cpu(), ids) and torch.equal(wd.cpu(), w)   # nothing masked any more
+        assert torch.equal(y, yr)
+    finally:
+        X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32),
+                       torch.zeros(0, dtype=torch.int32))
+
+
 def test_prefetch_claims_and_copies():
     H, I, K, E, S, L = 256, 128, 3, 16, 5, 1
     st = _store(H, I, K, E, S, L, seed=19)
