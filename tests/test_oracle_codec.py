@@ -8,7 +8,9 @@ n111_test.py, needs the B70 and an external NVMe store).  What it does state, an
   - the blob size 1,862,400 B at (H, I, K) = (2560, 640, 3) (kernels/moe-a8/exl3_moe.a8.sycl:7,
     experimental/n111-victim-ring/n111_test.py:21-23);
   - the word/shift form of tile_states (exl3_esimd.h:120-149) and the PLANAR4 view/permute of
-    plugin/exl3xpu/moe_offload.py:68-73.
+    plugin/exl3xpu/moe_offload.py:68-73;
+  - blobs packed by the reference's own pack_expert (plugin/exl3xpu/moe_offload.py:76-89), run on the CPU to make
+    tests/golden/ref_pack.npz.
 """
 import numpy as np
 import pytest
@@ -151,6 +153,28 @@ def test_synth_blob_identical_cpu_paths():
     assert not torch.equal(a, synth.make_blob(3, 18, 256, 128, 3))
     v = a[synth.blob_geometry(256, 128, 3, 3, 3)["suh_g"]:].view(torch.float16).float()
     assert torch.all(v[:256].abs() == 1.0)
+
+
+@pytest.mark.parametrize("K", [3, 5])
+def test_pack_matches_reference_packer(K):
+    """Blobs packed by the reference's own pack_expert / planar4 (tests/golden/ref_pack.npz, written by
+    tests/golden/make_ref_pack.py from the reference checkout): this build's pack_expert gives the same bytes, and the
+    oracle's blob reader decodes the reference's blob to the checkpoint trellis words' weights."""
+    import os
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_pack.npz"))
+
+    def tens(name):
+        return {f: torch.from_numpy(d[f"k{K}_{name}_{f}"]) for f in ("trellis", "suh", "svh")}
+
+    gate, up, down = tens("gate"), tens("up"), tens("down")
+    blob_ref = d[f"k{K}_blob"]
+    assert np.array_equal(moe_offload.pack_expert(gate, up, down, K).numpy(), blob_ref)
+    H, I = gate["trellis"].shape[0] * 16, gate["trellis"].shape[1] * 16
+    assert blob_ref.size == O.blob_bytes(H, I, K)
+    for proj, t, (k, n) in ((0, gate, (H, I)), (1, up, (H, I)), (2, down, (I, H))):
+        words = t["trellis"].view(torch.int32).numpy().view(np.uint32).reshape(k // 16, -1)
+        assert np.array_equal(O.blob_dequant(blob_ref, H, I, K, K, K, proj),
+                              O.dequant(words, k // 16, words.shape[1], 0, n // 16, K, False))
 
 
 def test_golden_fixtures_reproduce():
