@@ -1,10 +1,16 @@
-"""Two-tier EXL3 routed-expert store on B200: the drop-in for plugin/exl3xpu/moe_offload.py.
+"""Two-tier EXL3 routed-expert store on B200: the drop-in for the reference plugin's ExpertStore
+(plugin/exl3xpu/moe_offload.py:92-485; API listed at :14-31).
 
-Every expert of every MoE layer lives in pinned host memory (tier 1, readable by the GPU at the same address), a
-subset lives in device slots (tier 0, the expert cache, one arena shared by all layers).  Kernels address experts
-only through a per-layer int64 POINTER TABLE, so moving an expert between tiers is one 8-byte table write
-(moe_offload.py:1-31 in the reference).  The API, the blob format and the cache state tensors are the reference's;
-torch.xpu becomes torch.cuda and the ops come from libexl3b200.so (torch.ops.exl3b200_moe).
+Tier 1 is one pinned host arena per MoE layer ([E, blob] bytes, the GPU reads it at the host address over PCIe/C2C).
+Tier 0 is one device arena of n_slots blobs shared by all layers (the expert cache).  Kernels find an expert only
+through the per-(layer, expert) int64 pointer table ptrs_all, so moving an expert between tiers rewrites one table
+entry, and either pointer stays readable while a kernel may still hold the old one.
+
+Kept from the reference because callers and the op schemas depend on them: the constructor and method signatures,
+the names, shapes and dtypes of the device cache-state tensors (they are the arguments of moe_forward_cached and
+moe_prefetch), the blob format, and what each method guarantees.  The bookkeeping is this module's own: the host
+keeps a mirror of the device slot map shaped like the device tensors (slot_of[key] is a view into it), table
+updates are non-blocking copies from pinned memory, and prefill staging is a small double-buffer object.
 
 Expert blob (blob_bytes(H, I, K), 1,786,368 B at H=2048, I=768, K=3):
   gate|up trellis (u32 [H/16][2I/16][8K], PLANAR4) | down trellis ([I/16][H/16][8K], PLANAR4) |
@@ -12,8 +18,12 @@ Expert blob (blob_bytes(H, I, K), 1,786,368 B at H=2048, I=768, K=3):
 """
 from __future__ import annotations
 
+import contextlib
+import ctypes
+import re
 import threading
 
+import numpy as np
 import torch
 
 from . import ops as _ops
@@ -29,216 +39,317 @@ def ops():
 
 
 def s64(p: int) -> int:
-    return p - (1 << 64) if p >= (1 << 63) else p
+    """An address as the signed 64-bit value an int64 pointer table holds."""
+    return ctypes.c_int64(p).value
 
 
+# ------------------------------------------------------------------------------------------------ blob packing
 def planar4(tr: torch.Tensor, K: int) -> torch.Tensor:
-    """int16 trellis [rows, tiles, 16K] -> int32 words in PLANAR4 order (moe_offload.py:68-73).  Odd K: D = K planes of
-    8 periods per tile; even K (D = 1) is already planar, so the words are returned in checkpoint order."""
-    r, n, _ = tr.shape
-    w = tr.contiguous().view(torch.int32)
+    """Checkpoint trellis (int16 [rows, tiles, 16K]) -> its int32 words in PLANAR4 order (moe_offload.py:68-73).
+
+    A tile holds 8 periods of K words, period g's word i at 8K-index K*g + i.  For odd K, every run of 4 tiles along a
+    row is stored plane-major: [plane i][tile j][period g].  Even K (one word per plane) is planar already, so its
+    words keep checkpoint order."""
+    rows, tiles, _ = tr.shape
+    words = tr.contiguous().view(torch.int32)
     if K % 2 == 0:
-        return w.view(r, n, 8 * K)
-    if n % 4:
+        return words.view(rows, tiles, 8 * K)
+    if tiles % 4:
         raise ValueError("planar4: tiles per row must be a multiple of 4")
-    w = w.view(r, n // 4, 4, 8, K)                 # [row, group, tile, period g, plane i]
-    return w.permute(0, 1, 4, 2, 3).contiguous()   # [row, group, plane i, tile, g]
+    by_group = words.unflatten(1, (tiles // 4, 4)).unflatten(3, (8, K))   # [row, group, tile j, period g, plane i]
+    return by_group.movedim(4, 2).contiguous()                             # [row, group, plane i, tile j, period g]
+
+
+def _bytes(t: torch.Tensor) -> torch.Tensor:
+    return t.contiguous().view(torch.uint8).reshape(-1)
 
 
 def pack_expert(gate: dict, up: dict, down: dict, K: int, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Checkpoint tensors {trellis, suh, svh} of one expert -> blob (moe_offload.py:76-89).  K is the bit width of
-    gate/up/down; a mixed expert packs each tensor with its own K (trellis.shape[2] // 16)."""
-    b = lambda z: z.contiguous().view(torch.uint8).flatten()   # noqa: E731
-    kg = gate["trellis"].shape[2] // 16
-    ku = up["trellis"].shape[2] // 16
-    kd = down["trellis"].shape[2] // 16
+    """One expert's checkpoint tensors {trellis, suh, svh} -> its blob (moe_offload.py:76-89): a new uint8 CPU tensor,
+    or written into `out` (any device, exactly blob-sized).  Each projection's bit width is read from its trellis
+    (16K int16 per tile), so K is only a label; gate and up of different widths are packed per k-row as the gate
+    tiles (Kg) followed by the up tiles (Ku)."""
+    kg, ku, kd = (p["trellis"].shape[2] // 16 for p in (gate, up, down))
     if kg == ku:
-        gu = b(planar4(torch.cat([gate["trellis"], up["trellis"]], dim=1), kg))
-    else:   # per k-row: gate tiles (Kg) then up tiles (Ku)
-        pg = planar4(gate["trellis"], kg).reshape(gate["trellis"].shape[0], -1)
-        pu = planar4(up["trellis"], ku).reshape(up["trellis"].shape[0], -1)
-        gu = b(torch.cat([pg, pu], dim=1))
-    parts = [gu, b(planar4(down["trellis"], kd)), b(gate["suh"].half()), b(up["suh"].half()),
-             b(gate["svh"].half()), b(up["svh"].half()), b(down["suh"].half()), b(down["svh"].half())]
+        gate_up = planar4(torch.cat((gate["trellis"], up["trellis"]), dim=1), kg)
+    else:
+        gate_up = torch.cat((planar4(gate["trellis"], kg).flatten(1), planar4(up["trellis"], ku).flatten(1)), dim=1)
+    scales = [p[name].to(torch.float16) for name in ("suh", "svh") for p in (gate, up)]   # suh_g suh_u svh_g svh_u
+    sections = [_bytes(gate_up), _bytes(planar4(down["trellis"], kd))] + [_bytes(s) for s in scales] + \
+               [_bytes(down["suh"].to(torch.float16)), _bytes(down["svh"].to(torch.float16))]
     if out is None:
-        return torch.cat(parts)
-    o = 0
-    for p in parts:
-        out[o:o + p.numel()].copy_(p)
-        o += p.numel()
-    assert o == out.numel(), (o, out.numel())
+        return torch.cat(sections)
+    sizes = [s.numel() for s in sections]
+    if out.numel() != sum(sizes):
+        raise ValueError(f"pack_expert: the blob has {sum(sizes)} bytes, out has {out.numel()}")
+    for dst, src in zip(out.view(-1).split(sizes), sections):
+        dst.copy_(src)
     return out
 
 
+# ------------------------------------------------------------------------------------------------ device helpers
+class _Done:
+    """Event stand-in for a CPU store (tests): CPU work is synchronous, so every event has completed."""
+
+    def query(self) -> bool:
+        return True
+
+    def synchronize(self) -> None:
+        pass
+
+
+def _current(dev: torch.device):
+    return torch.cuda.current_stream(dev) if dev.type == "cuda" else None
+
+
+def _on(stream):
+    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+
+def _record(stream):
+    if stream is None:
+        return _Done()
+    ev = torch.cuda.Event()
+    ev.record(stream)
+    return ev
+
+
+def _wait(stream, ev) -> None:
+    if stream is not None and not isinstance(ev, _Done):
+        stream.wait_event(ev)
+
+
+def _as_route(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """The tensor itself when it is already contiguous `dtype` (so in-place rewrites by the cached op reach the
+    caller), else a contiguous converted copy."""
+    return t.contiguous().to(dtype)
+
+
+_LAYER_NO = re.compile(r"layers\.(\d+)\.")
+
+
+def _model_order(keys) -> list:
+    """Regular MoE layers in model order (the number after "layers."; keys without one last, in add order);
+    multi-token-prediction layers ("mtp." keys) are left out.  Layers may be added out of order as their checkpoint
+    shards load, so add order is not model order."""
+    def number(k):
+        m = _LAYER_NO.search(str(k))
+        return int(m.group(1)) if m else 1 << 30
+    return sorted((k for k in keys if not str(k).startswith("mtp.")), key=number)
+
+
+class _Staging:
+    """Double-buffered layer streaming for prefill (moe_offload.py:348-456): two device buffers of E blobs, a copy
+    stream, and per staged layer (buffer, pointer table, copy-done event)."""
+
+    def __init__(self, dev: torch.device):
+        self.stream = torch.cuda.Stream(dev) if dev.type == "cuda" else None
+        self.staged: dict = {}            # key -> (buffer, table, ready event), staged and not yet computed
+        self.busy = [None, None]          # per buffer: event after which its last reader has finished
+        self.order: list = []             # regular layers in model order
+        self.n_keys = -1
+        self.tick = None                  # cache tick when the tables were last validated
+
+    def in_buffer(self, buf: int) -> list:
+        return [k for k, (b, _, _) in self.staged.items() if b == buf]
+
+
+# ------------------------------------------------------------------------------------------------ the store
 class ExpertStore:
+    """Routed experts of up to max_layers MoE layers (n_experts each, H x I, K bits), n_slots of them in VRAM."""
+
     def __init__(self, H: int, I: int, K: int, n_experts: int, n_slots: int, device=None, max_layers: int = 64):
         self.H, self.I, self.K, self.E = H, I, K, n_experts
+        self.n_slots, self.max_layers = n_slots, max_layers
         self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.X = ops()
         self.blob = int(self.X.blob_bytes(H, I, K))
-        self.n_slots = n_slots
-        self.max_layers = max_layers
         self.slots = torch.empty((n_slots, self.blob), dtype=torch.uint8, device=self.dev) if n_slots else None
-        self.slot_owner: list = [None] * n_slots
-        self.free_slots = list(range(n_slots - 1, -1, -1))
-        self.host: dict = {}
-        self.layer_index: dict = {}
-        self.slot_of: dict = {}
-        self._host_ptr: dict = {}
-        self._stage = [None, None]
-        self._slot_ready_ev: dict = {}
-        LE = max_layers * n_experts
-        d = self.dev
-        self.ptrs_all = torch.zeros(LE, dtype=torch.int64, device=d)
-        self.slot_of_dev = torch.full((LE,), -1, dtype=torch.int32, device=d)
-        self.slot_key = torch.full((n_slots,), -1, dtype=torch.int32, device=d)
-        self.slot_last = torch.full((n_slots,), -1, dtype=torch.int32, device=d)
-        self.tick = torch.zeros(1, dtype=torch.int32, device=d)
-        self.host_base = torch.zeros(max_layers, dtype=torch.int64, device=d)
-        self.fill_all = torch.zeros(LE, dtype=torch.int64, device=d)
-        self.fill_list = torch.zeros(1 + n_experts, dtype=torch.int32, device=d)
-        self.pf_list = torch.zeros(1 + n_experts, dtype=torch.int32, device=d)
-        self.pf_slot = torch.zeros(n_experts, dtype=torch.int32, device=d)
-        self.pend = torch.zeros(max_layers * 35, dtype=torch.int32, device=d)
-        self.done_seq = torch.zeros(0, dtype=torch.int32, device=d)
         self.slot_base = s64(self.slots.data_ptr()) if n_slots else 0
-        self._cache_used = False
+        self.layer_index: dict = {}       # key -> row of the device tables (add order)
+        self.host: dict = {}              # key -> pinned uint8 [E, blob], tier 1
+        self._host_ptr: dict = {}         # key -> CPU int64 [E], host address of each expert's blob
+        self.slot_of: dict = {}           # key -> CPU int32 [E] view of _mirror_slot: slot of each expert, -1 = host
+        # host mirror of the device placement, valid for static placement (make_resident / evict); the device-managed
+        # cache (forward_cached, prefetch) moves experts on the device, and the mirror is re-read before the next
+        # static operation
+        LE = max_layers * n_experts
+        self._mirror_slot = torch.full((LE,), -1, dtype=torch.int32)       # mirrors slot_of_dev
+        self._mirror_key = np.full(n_slots, -1, dtype=np.int64)             # mirrors slot_key
+        self._slot_ready_ev: dict = {}    # slot -> event after which readers of its previous expert are done
+        self._cache_used = False          # forward_cached / prefetch ran since the mirror was read
+        self._stage = [None, None]        # prefill staging buffers [E, blob], allocated on first use
+        self._staging: _Staging | None = None
+        # device cache state, the arguments of moe_forward_cached / moe_prefetch: name -> (entries, dtype, initial)
+        i32, i64 = torch.int32, torch.int64
+        state = {"ptrs_all": (LE, i64, 0),           # blob address of every (layer, expert): host copy or slot
+                 "slot_of_dev": (LE, i32, -1),       # slot of every (layer, expert), -1 = not in VRAM
+                 "slot_key": (n_slots, i32, -1),     # (layer * E + expert) held by each slot, -1 = free
+                 "slot_last": (n_slots, i32, -1),    # tick of each slot's last use (the LRU order)
+                 "tick": (1, i32, 0),                # cached MoE calls so far
+                 "host_base": (max_layers, i64, 0),  # each layer's host arena
+                 "fill_all": (LE, i64, 0),           # per (layer, expert) fill state of the cache step
+                 "fill_list": (1 + n_experts, i32, 0),
+                 "pf_list": (1 + n_experts, i32, 0),
+                 "pf_slot": (n_experts, i32, 0),
+                 "pend": (max_layers * 35, i32, 0),  # copy-engine prefetch state (schema argument)
+                 "done_seq": (0, i32, 0)}            # empty: no copy-engine prefetch commits
+        for name, (n, dtype, init) in state.items():
+            setattr(self, name, torch.full((n,), init, dtype=dtype, device=self.dev))
 
     # ---- layers
+    def _rows(self, key) -> slice:
+        li = self.layer_index[key]
+        return slice(li * self.E, (li + 1) * self.E)
+
     def add_layer(self, key, blobs: torch.Tensor | None = None) -> torch.Tensor:
+        """Allocate layer `key`'s host arena (filled from `blobs` [E, blob] when given) and point its table there."""
         li = len(self.layer_index)
         if li >= self.max_layers:
             raise RuntimeError(f"ExpertStore: more than max_layers={self.max_layers} MoE layers")
-        self.layer_index[key] = li
-        h = self.X.host_alloc(self.E * self.blob).view(self.E, self.blob)
+        arena = self.X.host_alloc(self.E * self.blob).view(self.E, self.blob)
         if blobs is not None:
-            h.copy_(blobs)
-        self.host[key] = h
-        base = s64(h.data_ptr())
-        self._host_ptr[key] = base + torch.arange(self.E, dtype=torch.int64) * self.blob
-        self.ptrs_all[li * self.E:(li + 1) * self.E].copy_(self._host_ptr[key])
+            arena.copy_(blobs)
+        base = s64(arena.data_ptr())
+        self.layer_index[key] = li
+        self.host[key] = arena
+        self._host_ptr[key] = torch.arange(self.E, dtype=torch.int64).mul_(self.blob).add_(base)
+        self.slot_of[key] = self._mirror_slot[li * self.E:(li + 1) * self.E]
+        self.ptrs_all[self._rows(key)].copy_(self._host_ptr[key])
         self.host_base[li] = base
-        self.slot_of[key] = torch.full((self.E,), -1, dtype=torch.int32)
-        return h
+        return arena
 
     def host_view(self, key) -> torch.Tensor:
         return self.host[key]
 
     def ptrs(self, key) -> torch.Tensor:
-        li = self.layer_index[key]
-        return self.ptrs_all[li * self.E:(li + 1) * self.E]
+        """Layer `key`'s int64 [E] pointer table (a view of ptrs_all: fixed address)."""
+        return self.ptrs_all[self._rows(key)]
 
     def slot_ptr(self, s: int) -> int:
         return self.slot_base + s * self.blob
 
+    @property
+    def free_slots(self) -> list:
+        """Free slots by the host mirror, in the order make_resident takes them (lowest first)."""
+        return np.flatnonzero(self._mirror_key < 0).tolist()
+
+    @property
+    def slot_owner(self) -> list:
+        """Per slot (key, expert) by the host mirror, None when free."""
+        by_row = {li: k for k, li in self.layer_index.items()}
+        return [None if c < 0 else (by_row[int(c) // self.E], int(c) % self.E) for c in self._mirror_key]
+
+    def _to_dev(self, values, dtype: torch.dtype) -> torch.Tensor:
+        """A small index/value list on the device, copied from pinned memory without a host sync; the copy is
+        ordered on the current stream (the pinned buffer is kept until it has run)."""
+        t = torch.tensor(values, dtype=dtype)
+        if self.dev.type != "cuda":
+            return t
+        return t.pin_memory().to(self.dev, non_blocking=True)
+
     # ---- static residency
     def make_resident(self, key, experts, stream=None) -> int:
-        """Copy experts into free device slots, then repoint the table and the device slot map, ordered on `stream`
-        (default: current stream).  Returns the number copied (moe_offload.py:154-185)."""
-        s_ = stream or torch.cuda.current_stream(self.dev)
+        """Copy `experts` of `key` that are not in VRAM into free slots, then point the table and the device slot map
+        at them, all ordered on `stream` (default: the current stream).  Returns the number copied
+        (moe_offload.py:154-185)."""
         self._resync()
-        so = self.slot_of[key]
         li = self.layer_index[key]
-        todo = [int(e) for e in experts if so[int(e)] < 0]
+        mine = self.slot_of[key]
+        todo = [e for e in dict.fromkeys(int(e) for e in experts) if mine[e] < 0]
         if not todo:
             return 0
-        es, sls = [], []
-        with torch.cuda.stream(s_):
-            for e in todo:
-                if not self.free_slots:
-                    raise RuntimeError("ExpertStore: no free slot (evict first or raise n_slots)")
-                sl = self.free_slots.pop()
-                ev = self._slot_ready_ev.pop(sl, None)
+        free = self.free_slots[:len(todo)]
+        if len(free) < len(todo):
+            raise RuntimeError(f"ExpertStore: {len(todo)} experts for {len(free)} free slots "
+                               "(evict first or raise n_slots)")
+        self.prefill_reset()
+        cs = stream if stream is not None else _current(self.dev)
+        codes = [li * self.E + e for e in todo]
+        with _on(cs):
+            for e, s in zip(todo, free):
+                ev = self._slot_ready_ev.pop(s, None)
                 if ev is not None:
-                    s_.wait_event(ev)
-                self.X.memcpy_async(self.slot_ptr(sl), s64(self.host[key][e].data_ptr()), self.blob)
-                self.slot_owner[sl] = (key, e)
-                so[e] = sl
-                es.append(e)
-                sls.append(sl)
-            d = self.dev
-            keys = torch.tensor([li * self.E + e for e in es], dtype=torch.int64)
-            slt = torch.tensor(sls, dtype=torch.int64)
-            self.ptrs_all.index_copy_(0, keys.to(d), (self.slot_base + slt * self.blob).to(d))
-            self.slot_of_dev.index_copy_(0, keys.to(d), slt.to(torch.int32).to(d))
-            self.slot_key.index_copy_(0, slt.to(d), keys.to(torch.int32).to(d))
-            self.slot_last.index_fill_(0, slt.to(d), 0)
+                    _wait(cs, ev)
+                self.X.memcpy_async(self.slot_ptr(s), int(self._host_ptr[key][e]), self.blob)
+            at = self._to_dev(codes, torch.int64)
+            sl = self._to_dev(free, torch.int64)
+            self.ptrs_all.index_copy_(0, at, sl * self.blob + self.slot_base)
+            self.slot_of_dev.index_copy_(0, at, sl.to(torch.int32))
+            self.slot_key.index_copy_(0, sl, at.to(torch.int32))
+            self.slot_last.index_fill_(0, sl, 0)
+        mine[todo] = torch.tensor(free, dtype=torch.int32)
+        self._mirror_key[free] = codes
         return len(todo)
 
     def evict(self, key, experts) -> None:
-        """Repoint to the host copy; the slot is reusable after the current stream's queued work."""
+        """Point `experts` of `key` back at their host copies; a freed slot is refilled only after the work queued on
+        the current stream so far (moe_offload.py:187-216)."""
         self._resync()
-        so = self.slot_of[key]
         li = self.layer_index[key]
-        es, sls = [], []
-        for e in experts:
-            e = int(e)
-            sl = int(so[e])
-            if sl < 0:
-                continue
-            es.append(e)
-            sls.append(sl)
-            so[e] = -1
-            self.slot_owner[sl] = None
-        if not es:
+        mine = self.slot_of[key]
+        gone = [e for e in dict.fromkeys(int(e) for e in experts) if mine[e] >= 0]
+        if not gone:
             return
-        d = self.dev
-        et = torch.tensor(es, dtype=torch.int64)
-        keys = (li * self.E + et).to(d)
-        slt = torch.tensor(sls, dtype=torch.int64).to(d)
-        self.ptrs_all.index_copy_(0, keys, self._host_ptr[key][et].to(d))
-        self.slot_of_dev.index_fill_(0, keys, -1)
-        self.slot_key.index_fill_(0, slt, -1)
-        self.slot_last.index_fill_(0, slt, -1)
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(self.dev))
-        for sl in sls:
-            self._slot_ready_ev[sl] = ev
-            self.free_slots.append(sl)
+        self.prefill_reset()
+        freed = mine[gone].tolist()
+        at = self._to_dev([li * self.E + e for e in gone], torch.int64)
+        sl = self._to_dev(freed, torch.int64)
+        self.ptrs_all.index_copy_(0, at, self._to_dev(self._host_ptr[key][gone].tolist(), torch.int64))
+        self.slot_of_dev.index_fill_(0, at, -1)
+        self.slot_key.index_fill_(0, sl, -1)
+        self.slot_last.index_fill_(0, sl, -1)
+        mine[gone] = -1
+        self._mirror_key[freed] = -1
+        done = _record(_current(self.dev))
+        for s in freed:
+            self._slot_ready_ev[s] = done
 
     def resident_count(self, key=None) -> int:
+        """Experts in VRAM by the host mirror (all layers when key is None)."""
         if key is None:
-            return sum(int((v >= 0).sum()) for v in self.slot_of.values())
+            return int((self._mirror_slot >= 0).sum())
         return int((self.slot_of[key] >= 0).sum())
 
     def device_resident_count(self, key) -> int:
-        li = self.layer_index[key]
-        return int((self.slot_of_dev[li * self.E:(li + 1) * self.E] >= 0).sum().item())
+        """Experts of `key` in VRAM by the device slot map (reads the device)."""
+        return int((self.slot_of_dev[self._rows(key)] >= 0).sum().item())
 
     # ---- compute
     @staticmethod
     def _rt(topk_ids, topk_w):
-        ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() else topk_ids.to(torch.int32).contiguous()
-        w = topk_w if topk_w.dtype == torch.float32 and topk_w.is_contiguous() else topk_w.to(torch.float32).contiguous()
-        return ids, w
+        """Routing as the ops take it: contiguous int32 ids and fp32 weights, the caller's own tensors when they
+        already are (the cached op may rewrite masked picks in place, and callers read that)."""
+        return _as_route(topk_ids, torch.int32), _as_route(topk_w, torch.float32)
 
     def forward(self, key, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, ptrs=None) -> torch.Tensor:
+        """Routed-MoE output of layer `key` through its table (or `ptrs`); weights applied, no shared expert."""
         ids, w = self._rt(topk_ids, topk_w)
         return self.X.moe_forward(x, ids, w, self.ptrs(key) if ptrs is None else ptrs, self.I, self.K, self.E)
 
     def forward_cached(self, key, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor,
                        max_fill: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Decode with the device-managed LRU cache: misses are copied from host into their LRU slot and the table is
-        repointed within the call (no host sync, graph-safe).  With the tier on, picks in neither VRAM nor RAM are
-        rewritten in place to (safe expert, weight 0) and logged to the miss ring."""
+        """Decode through the device-managed LRU cache (moe_offload.py:239-249): hits read their slot, up to max_fill
+        misses are copied from host into LRU slots and the table is repointed within the call, with no host sync (the
+        call can be captured in a CUDA graph).  With the RAM tier on, picks in neither VRAM nor RAM are rewritten in
+        place to (safe expert, weight 0) and logged to the miss ring.  `out` (this build's extension) takes the
+        output in a caller buffer: the same computation without the torch op dispatch."""
         ids, w = self._rt(topk_ids, topk_w)
         self._cache_used = True
-        if out is not None:   # extension: write into a caller buffer (same computation, no torch op dispatch)
-            return _ops._moe_forward_cached_impl(x, ids, w, self.ptrs_all, self.layer_index[key], self.slot_of_dev,
-                                                 self.slot_key, self.slot_last, self.tick, self.host_base, self.slot_base,
-                                                 self.fill_all, self.fill_list, self.E if max_fill is None else max_fill,
-                                                 self.I, self.K, self.E, self.pend, self.done_seq, out=out)
-        return self.X.moe_forward_cached(x, ids, w, self.ptrs_all, self.layer_index[key], self.slot_of_dev,
-                                         self.slot_key, self.slot_last, self.tick, self.host_base, self.slot_base,
-                                         self.fill_all, self.fill_list, self.E if max_fill is None else max_fill,
-                                         self.I, self.K, self.E, self.pend, self.done_seq)
+        args = (x, ids, w, self.ptrs_all, self.layer_index[key], self.slot_of_dev, self.slot_key, self.slot_last,
+                self.tick, self.host_base, self.slot_base, self.fill_all, self.fill_list,
+                self.E if max_fill is None else max_fill, self.I, self.K, self.E, self.pend, self.done_seq)
+        if out is not None:
+            return _ops._moe_forward_cached_impl(*args, out=out)
+        return self.X.moe_forward_cached(*args)
 
     def prefetch(self, key, ids: torch.Tensor, max_fill: int = 16) -> None:
-        """Claim LRU slots for predicted experts of `key` and copy them from host on the CURRENT stream (use a side
-        stream that waited for the previous MoE call).  The tick is not advanced, so the last call's slots stay."""
+        """Claim LRU slots for the predicted experts `ids` of `key` and copy them from host, on the CURRENT stream
+        (a side stream that waited for the previous MoE call; the compute stream waits for it before the next).  The
+        tick is not advanced, so the slots of the last MoE call stay (moe_offload.py:251-262)."""
         if not self.n_slots:
             return
-        ids = ids if ids.dtype == torch.int32 and ids.is_contiguous() else ids.to(torch.int32).contiguous()
+        ids = _as_route(ids, torch.int32)
         self._cache_used = True
         self.X.moe_prefetch(ids.flatten(), self.ptrs_all, self.layer_index[key], self.slot_of_dev, self.slot_key,
                             self.slot_last, self.tick, self.host_base, self.slot_base, self.pf_list, self.pf_slot,
@@ -246,129 +357,104 @@ class ExpertStore:
 
     # ---- prefill staging
     def stage_layer(self, key, buf: int, stream) -> torch.Tensor:
-        """Copy every non-resident expert of `key` into staging buffer `buf` on `stream`; returns the pointer table to
-        pass to forward(ptrs=...) once `stream` has been waited on (moe_offload.py:305-329)."""
+        """Queue on `stream` the copy of every expert of `key` that is not in VRAM into staging buffer `buf` (0 or 1),
+        runs of consecutive experts as one copy; returns the layer's pointer table for forward(ptrs=...), valid once
+        `stream` has been waited on: slots for resident experts, the staging buffer for the rest
+        (moe_offload.py:305-329)."""
         if self._stage[buf] is None:
             self._stage[buf] = torch.empty((self.E, self.blob), dtype=torch.uint8, device=self.dev)
-        st = self._stage[buf]
+        base = s64(self._stage[buf].data_ptr())
         self._resync()
-        so = self.slot_of[key]
-        miss = (so < 0).nonzero().flatten().tolist()
-        with torch.cuda.stream(stream):
-            i = 0
-            while i < len(miss):
-                j = i
-                while j + 1 < len(miss) and miss[j + 1] == miss[j] + 1:
-                    j += 1
-                n = j - i + 1
-                self.X.memcpy_async(s64(st[miss[i]].data_ptr()), s64(self.host[key][miss[i]].data_ptr()), n * self.blob)
-                i = j + 1
-        sp = s64(st.data_ptr()) + torch.arange(self.E, dtype=torch.int64) * self.blob
-        if self.n_slots:
-            dp = self.slot_base + so.clamp_min(0).to(torch.int64) * self.blob
-            sp = torch.where(so >= 0, dp, sp)
-        return sp.to(self.dev)
+        mine = self.slot_of[key]
+        missing = np.flatnonzero(mine.numpy() < 0)
+        if missing.size:
+            runs = np.split(missing, np.flatnonzero(np.diff(missing) != 1) + 1)
+            src = self._host_ptr[key]
+            with _on(stream):
+                for run in runs:
+                    e0 = int(run[0])
+                    self.X.memcpy_async(base + e0 * self.blob, int(src[e0]), len(run) * self.blob)
+        table = torch.arange(self.E, dtype=torch.int64).mul_(self.blob).add_(base)
+        held = mine >= 0
+        table[held] = mine[held].to(torch.int64) * self.blob + self.slot_base
+        return self._to_dev(table.tolist(), torch.int64)
 
     def reset_cache(self) -> None:
-        """Empty every slot and repoint all tables to host memory (waits for queued work)."""
-        torch.cuda.current_stream(self.dev).synchronize()
-        for key, li in self.layer_index.items():
-            self.ptrs_all[li * self.E:(li + 1) * self.E].copy_(self._host_ptr[key])
-            self.slot_of[key].fill_(-1)
-        self.slot_of_dev.fill_(-1)
-        self.slot_key.fill_(-1)
-        self.slot_last.fill_(-1)
+        """Empty every slot and point every table at host memory (waits for the current stream's queued work)."""
+        cs = _current(self.dev)
+        if cs is not None:
+            cs.synchronize()
+        for key in self.layer_index:
+            self.ptrs_all[self._rows(key)].copy_(self._host_ptr[key])
+        for t in (self.slot_of_dev, self.slot_key, self.slot_last):
+            t.fill_(-1)
         self.fill_all.zero_()
         self.pend.zero_()
-        self.slot_owner = [None] * self.n_slots
-        self.free_slots = list(range(self.n_slots - 1, -1, -1))
+        self._mirror_slot.fill_(-1)
+        self._mirror_key.fill(-1)
         self._slot_ready_ev.clear()
         self._cache_used = False
+        self.prefill_reset()
 
     def forward_prefill_staged(self, key, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor) -> torch.Tensor:
-        """Prefill-size MoE for `key` from a device staging buffer, double-buffered across layers on a side stream
-        (moe_offload.py:348-437): the layer's non-resident experts are copied H2D (normally while the previous
-        layer computed), then the next layer starts staging into the other buffer."""
-        if not hasattr(self, "_pf"):
-            self._pf = {"stream": torch.cuda.Stream(self.dev), "buf_of": {}, "ready": {}, "free": [None, None],
-                        "order": None}
-        pf = self._pf
-        if pf["order"] is None or len(pf["order"]) != len(self.layer_index):
-            pf["order"] = list(self.layer_index)
-            import re as _re
+        """Prefill-size MoE of layer `key` from a staging buffer (moe_offload.py:348-437).  The layer's experts that
+        are not in VRAM were normally copied on the copy stream while the previous layer computed; after queueing this
+        layer's compute, the next layer in model order (wrapping to the first: chunked prefill runs forwards back to
+        back) is staged into the other buffer.
 
-            def _lid(k):
-                m = _re.search(r"layers\.(\d+)\.", str(k))
-                return int(m.group(1)) if m else 1 << 30
-            pf["layers"] = sorted((k for k in pf["order"] if not str(k).startswith("mtp.")), key=_lid)
-        cs = torch.cuda.current_stream(self.dev)
-        if pf["layers"] and key == pf["layers"][0]:
-            torch.cuda.synchronize(self.dev)
-            t = int(self.tick.item())
-            if pf.get("tick") != t or self._cache_used:
+        At the first layer of a forward the host synchronises the device: decode (graph replays) may have moved
+        cache slots since the tables were staged, so when the cache tick moved (or cached calls ran) the placement
+        mirror is re-read and pre-staged tables are dropped."""
+        if self._staging is None:
+            self._staging = _Staging(self.dev)
+        sg = self._staging
+        if sg.n_keys != len(self.layer_index):
+            sg.order, sg.n_keys = _model_order(self.layer_index), len(self.layer_index)
+        if sg.order and key == sg.order[0]:
+            if self.dev.type == "cuda":
+                torch.cuda.synchronize(self.dev)
+            tick = int(self.tick.item())
+            if tick != sg.tick or self._cache_used:
                 self.sync_mirror()
-                self._cache_used = False
-                pf["buf_of"].clear()
-                pf["ready"].clear()
-                pf["tick"] = t
-        if key not in pf["buf_of"]:
-            used = {b for b, _ in pf["buf_of"].values()}
-            self._stage_into(key, 0 if 0 not in used else 1)
-        buf, table = pf["buf_of"].pop(key)
-        rdy = pf["ready"].pop(key)
-        cs.wait_event(rdy)
-        ids, w = self._rt(topk_ids, topk_w)
-        y = self.X.moe_forward(x, ids, w, table, self.I, self.K, self.E)
-        ev = torch.cuda.Event()
-        ev.record(cs)
-        pf["free"][buf] = ev
-        layers = pf["layers"]
-        pos = layers.index(key) if key in layers else -1
-        if pos >= 0 and layers:
-            nxt = layers[(pos + 1) % len(layers)]
-            if nxt not in pf["buf_of"] and nxt != key:
+                sg.staged.clear()
+                sg.tick = tick
+        if key not in sg.staged:
+            self._stage_into(key, 1 if sg.in_buffer(0) else 0)
+        buf, table, ready = sg.staged.pop(key)
+        cs = _current(self.dev)
+        _wait(cs, ready)
+        y = self.forward(key, x, topk_ids, topk_w, ptrs=table)
+        sg.busy[buf] = _record(cs)
+        if key in sg.order:
+            nxt = sg.order[(sg.order.index(key) + 1) % len(sg.order)]
+            if nxt != key and nxt not in sg.staged:
                 self._stage_into(nxt, 1 - buf)
         return y
 
     def _stage_into(self, key, buf: int) -> None:
-        pf = self._pf
-        st = pf["stream"]
-        for k_ in [k_ for k_, (b_, _) in pf["buf_of"].items() if b_ == buf]:
-            pf["buf_of"].pop(k_)
-            pf["ready"].pop(k_, None)
-        if pf["free"][buf] is not None:
-            st.wait_event(pf["free"][buf])
-            pf["free"][buf] = None
-        table = self.stage_layer(key, buf, st)
-        ev = torch.cuda.Event()
-        ev.record(st)
-        pf["buf_of"][key] = (buf, table)
-        pf["ready"][key] = ev
+        """Stage `key` into buffer `buf` on the copy stream, after that buffer's last reader; a layer staged there
+        earlier and not computed yet is dropped (its copy is about to be overwritten)."""
+        sg = self._staging
+        for k in sg.in_buffer(buf):
+            del sg.staged[k]
+        if sg.busy[buf] is not None:
+            _wait(sg.stream, sg.busy[buf])
+            sg.busy[buf] = None
+        table = self.stage_layer(key, buf, sg.stream)
+        sg.staged[key] = (buf, table, _record(sg.stream))
 
     def prefill_reset(self) -> None:
-        """Drop pre-staged layers (their tables hold slot pointers valid only until the next cache update)."""
-        if hasattr(self, "_pf") and self._pf["buf_of"]:
-            self._pf["buf_of"].clear()
-            self._pf["ready"].clear()
+        """Drop pre-staged layers: their tables hold slot pointers that are valid only until the placement changes."""
+        if self._staging is not None:
+            self._staging.staged.clear()
 
     def sync_mirror(self) -> None:
-        """Rebuild the CPU mirror (slot_of, slot_owner, free list) from the device cache state (syncs)."""
-        sk = self.slot_key.cpu()
-        sod = self.slot_of_dev.cpu()
-        keys = {li: key for key, li in self.layer_index.items()}
-        for key, li in self.layer_index.items():
-            self.slot_of[key] = sod[li * self.E:(li + 1) * self.E].clone()
-        self.slot_owner = [None] * self.n_slots
-        free = []
-        for sl in range(self.n_slots):
-            k = int(sk[sl])
-            if k < 0:
-                free.append(sl)
-            else:
-                self.slot_owner[sl] = (keys[k // self.E], k % self.E)
-        self.free_slots = free[::-1]
+        """Re-read the host mirror of the placement (slot_of, free slots, owners) from the device slot map: a
+        device-to-host read that synchronises the current stream, for static placement, never in the decode loop."""
+        self._mirror_slot.copy_(self.slot_of_dev.cpu())
+        self._mirror_key[:] = self.slot_key.cpu().numpy()
+        self._cache_used = False
 
     def _resync(self) -> None:
         if self._cache_used:
             self.sync_mirror()
-            self._cache_used = False
