@@ -9,26 +9,28 @@ The reference runs this loop as NvTierAsync.step and its admission-controlled va
     lands at ring[1 + n % cap];
   * the victim write-back (exl3b_victim_copy) copies an evicted VRAM expert to its host slot and sets ram_res[key].
 
-TierHost.step() runs once per decode step, after the step has been queued:
+The host keeps one state per key (absent, fetching, resident since step t) and a pinned snapshot of the device's
+ram_res, ring and slot_of.  The snapshot is queued at the end of every step(), behind that step's own flag writes, and
+read at the start of the next one, after the next decode step has been queued: reading it waits for the previous
+decode step only, and it never predates the host's own writes, so a flag that differs from the host's state was set
+by the device.  step(), once per decode step after the step's kernels are queued:
 
-  1. snapshot: the device's ram_res, ring and slot_of are copied to host buffers (pinned on a GPU) behind an event,
-     and used one step later, so the step itself is never synchronised;
-  2. flags: keys the device flagged since (victim write-back) and fills reported complete (fill_done) become
-     resident, aged with the current step;
-  3. misses: the keys logged since the previous snapshot (the last cap of them when more were logged) that are
-     neither resident nor being fetched are the wanted keys, most-logged first;
-  4. budget (resident + in flight + wanted <= budget): resident keys are dropped -- first those that also sit in
-     VRAM, then the others resident for at least min_age steps, oldest first; pinned keys never;
-  5. admission: wanted keys are handed to fetch(key) while the budget has room and fewer than max_inflight are in
-     flight; the rest stay masked and come back through the ring on their next miss;
-  6. upload: the flags that changed are written to the device (index_copy_ on the current stream); a dropped key's
-     host copy goes to release(key) once the device has run a whole step after that flag clear (so a snapshot
-     shows any victim write-back of the key in that step) -- unless the device flagged the key again or the key
-     was wanted and fetched again meanwhile.
+  1. absorbs what happened since: keys the device flagged (victim write-backs) and keys whose fetch reported
+     fill_done become resident at this step;
+  2. releases dropped keys once a snapshot taken after a whole decode step past their flag clear has been read (it
+     shows any write-back of the key in that step, which makes it resident again instead);
+  3. reads the keys logged to the miss ring since the previous snapshot (the last cap of them when more were logged);
+     the absent ones are wanted, most-logged first, lower key first on ties;
+  4. makes room for them, resident + fetching + wanted <= budget, by dropping resident keys that are not pinned:
+     those whose expert also sits in VRAM first, then those resident for at least min_age steps, oldest first in each
+     group;
+  5. hands wanted keys to fetch(key) while the budget has room and fewer than max_inflight are fetching; the rest stay
+     masked and come back through the ring on their next miss;
+  6. writes the flags that differ from the snapshot (index_copy_ on the current stream), then queues the next snapshot.
 
 fetch(key) starts making the key's host copy valid (the caller's storage: a file read, a copy from another tier) and
-reports completion with fill_done(key), from any thread.  Device tensors may also be CPU tensors (tests): copies are
-then synchronous and events complete at once.
+reports completion with fill_done(key), from any thread.  The device tensors may be CPU tensors (tests): copies are
+then synchronous.
 """
 from __future__ import annotations
 
@@ -38,15 +40,35 @@ import queue
 import numpy as np
 import torch
 
+ABSENT, FETCHING, RESIDENT = 0, 1, 2
 
-class _Complete:
-    """Event stand-in for CPU tensors: their copies are synchronous."""
 
-    def query(self) -> bool:
-        return True
+class _Snapshot:
+    """One pinned host copy of the device's (ram_res, ring, slot_of), queued behind an event."""
 
-    def synchronize(self) -> None:
-        pass
+    def __init__(self, ram_res: torch.Tensor, ring: torch.Tensor, slot_of: torch.Tensor, n: int):
+        self.cuda = ram_res.device.type == "cuda"
+        self.src = (ram_res[:n], ring, slot_of[:n])
+        self.host = tuple(torch.empty(t.numel(), dtype=t.dtype, pin_memory=self.cuda) for t in self.src)
+        self.ready = None       # None before the first queue(); then an event, or True on the CPU
+
+    def queue(self) -> None:
+        for dst, src in zip(self.host, self.src):
+            dst.copy_(src, non_blocking=self.cuda)
+        if self.cuda:
+            self.ready = torch.cuda.Event()
+            self.ready.record(torch.cuda.current_stream(self.src[0].device))
+        else:
+            self.ready = True
+
+    def read(self):
+        """(flags, ring, in_vram) as numpy views of the host copy, valid until the next queue(); None before any."""
+        if self.ready is None:
+            return None
+        if self.cuda:
+            self.ready.synchronize()
+        flags, ring, slot = (t.numpy() for t in self.host)
+        return flags != 0, ring, slot >= 0
 
 
 class TierHost:
@@ -56,8 +78,7 @@ class TierHost:
             raise RuntimeError("exl3b200 TierHost: uint8 ram_res, int32 ring, int32 slot_of")
         if ring.numel() < 2 or slot_of.numel() < ram_res.numel():
             raise RuntimeError("exl3b200 TierHost: the ring needs >= 1 entry and slot_of one entry per key")
-        self.ram_res, self.ring, self.slot_of = ram_res, ring, slot_of
-        self.dev = ram_res.device
+        self.ram_res = ram_res
         self.n = ram_res.numel()
         self.cap = ring.numel() - 1
         self.budget = int(budget)
@@ -66,152 +87,125 @@ class TierHost:
         self.pinned = np.zeros(self.n, dtype=bool) if pinned is None else np.asarray(pinned, dtype=bool).copy()
         self.min_age = int(min_age)
         self.max_inflight = max_inflight
-        self.res = ram_res.cpu().numpy().astype(np.uint8)          # the host's flags (what it last uploaded)
-        self.age = np.zeros(self.n, dtype=np.int64)
-        self.inflight = np.zeros(self.n, dtype=bool)
+        self.state = np.where(ram_res.cpu().numpy() != 0, RESIDENT, ABSENT).astype(np.int8)
+        self.since = np.zeros(self.n, dtype=np.int64)     # step at which a resident key became resident
         self.tick = 0
         self.ring_seen = int(ring[0].item())
-        pin = self.dev.type == "cuda"
-        self._snap = [{"res": torch.empty(self.n, dtype=torch.uint8, pin_memory=pin),
-                       "ring": torch.empty(ring.numel(), dtype=torch.int32, pin_memory=pin),
-                       "slot": torch.empty(self.n, dtype=torch.int32, pin_memory=pin)} for _ in range(2)]
-        self._snap_ev = [None, None]
-        self._k = 0
-        self._last_diff = None      # (keys, values) uploaded by the previous step
-        self._clears = []           # [(event, tick, keys)] dropped keys awaiting release
+        self._snap = _Snapshot(ram_res, ring, slot_of, self.n)
+        self._dropped: list = []                          # [(step of the drop, keys)] awaiting release
         self._done = queue.SimpleQueue()
         self.stats = collections.Counter()
 
-    # ---------------------------------------------------------------- storage side
+    @property
+    def res(self) -> np.ndarray:
+        """The host's resident flags (uint8 per key), what it last wrote to ram_res."""
+        return (self.state == RESIDENT).astype(np.uint8)
+
+    def resident(self) -> int:
+        return int(np.count_nonzero(self.state == RESIDENT))
+
     def fill_done(self, key: int) -> None:
         """The host copy of key is valid (thread-safe)."""
         self._done.put(int(key))
 
     # ---------------------------------------------------------------- per step
-    def _event(self):
-        if self.dev.type == "cuda":
-            ev = torch.cuda.Event()
-            ev.record(torch.cuda.current_stream(self.dev))
-            return ev
-        return _Complete()
-
-    def _upload(self, keys: np.ndarray, vals: np.ndarray) -> None:
-        pin = self.dev.type == "cuda"
-        idx = torch.from_numpy(keys.astype(np.int64))
-        val = torch.from_numpy(vals.astype(np.uint8))
-        if pin:
-            idx, val = idx.pin_memory(), val.pin_memory()
-        self.ram_res.index_copy_(0, idx.to(self.dev, non_blocking=True), val.to(self.dev, non_blocking=True))
-
     def step(self) -> int:
         """One decode step's bookkeeping (see the module docstring).  Returns the number of misses logged in the
-        snapshot it consumed."""
+        snapshot it read."""
         self.tick += 1
-        k = self._k
-        self._k ^= 1
-        snap = self._snap[k]
-        snap["res"].copy_(self.ram_res[: self.n], non_blocking=True)
-        snap["ring"].copy_(self.ring, non_blocking=True)
-        snap["slot"].copy_(self.slot_of[: self.n], non_blocking=True)
-        self._snap_ev[k] = self._event()
-        j = k ^ 1
-        if self._snap_ev[j] is None:   # first step: nothing to consume yet
-            self.stats["steps"] += 1
-            return 0
-        self._snap_ev[j].synchronize()   # queued before this step's work: normally complete already
-        res_d = self._snap[j]["res"].numpy().copy()
-        if self._last_diff is not None:   # the device as of the previous upload
-            dk, dv = self._last_diff
-            res_d[dk] = dv
-        ring = self._snap[j]["ring"].numpy()
-        vram = self._snap[j]["slot"].numpy() >= 0
+        snap = self._snap.read()
+        logged = 0
+        if snap is not None:
+            flags, ring, in_vram = snap
+            self._absorb(flags)
+            self._release_dropped()
+            want, logged = self._wanted(ring)
+            dropped = self._make_room(len(want), in_vram)
+            self._admit(want)
+            self._write_flags(flags)
+            if dropped.size:
+                self._dropped.append((self.tick, dropped))
+        self._snap.queue()
+        self.stats["steps"] += 1
+        return logged
 
-        # dropped keys: the snapshot consumed now was taken a step after their clear was queued (tick + 1), so it
-        # shows a victim write-back of the key in that step; release the host copy unless the key is back
-        pending = []
-        for ev, tq, keys in self._clears:
-            if self.tick < tq + 2 or not ev.query():
-                pending.append((ev, tq, keys))
-                continue
-            for key in keys.tolist():
-                if res_d[key] or self.res[key] or self.inflight[key]:
-                    self.stats["release_rescued"] += 1
-                else:
-                    self.release(key)
-                    self.stats["released"] += 1
-        self._clears = pending
+    def _become_resident(self, keys) -> None:
+        self.state[keys] = RESIDENT
+        self.since[keys] = self.tick
 
-        res = self.res.copy()
-        flagged = (res_d == 1) & (res == 0)   # victim write-back
-        res[flagged] = 1
-        self.age[flagged] = self.tick
-        self.stats["victims_kept"] += int(flagged.sum())
+    def _absorb(self, flags: np.ndarray) -> None:
+        flagged = np.flatnonzero(flags & (self.state != RESIDENT))     # victim write-backs
+        self._become_resident(flagged)
+        self.stats["victims_kept"] += flagged.size
+        filled = []
         while True:
             try:
-                key = self._done.get_nowait()
+                filled.append(self._done.get_nowait())
             except queue.Empty:
                 break
-            res[key] = 1
-            self.age[key] = self.tick
-            self.inflight[key] = False
+        if filled:
+            self._become_resident(np.asarray(filled, dtype=np.int64))
 
-        # misses logged since the previous snapshot
-        cnt = int(ring[0])
-        new = cnt - self.ring_seen
+    def _release_dropped(self) -> None:
+        waiting = []
+        for when, keys in self._dropped:
+            # the snapshot read now was queued at the end of step tick - 1, after decode step tick - 1 >= when + 1
+            if self.tick < when + 2:
+                waiting.append((when, keys))
+                continue
+            back = self.state[keys] != ABSENT
+            self.stats["release_rescued"] += int(back.sum())
+            for key in keys[~back].tolist():
+                self.release(key)
+                self.stats["released"] += 1
+        self._dropped = waiting
+
+    def _wanted(self, ring: np.ndarray):
+        count = int(ring[0])
+        new = count - self.ring_seen
+        self.ring_seen = count
         if new > self.cap:
             self.stats["ring_overflow"] += new - self.cap
             new = self.cap
-        want = np.zeros(0, dtype=np.int64)
-        if new > 0:
-            keys = ring[1 + np.arange(cnt - new, cnt) % self.cap].astype(np.int64)
-            keys = keys[(keys >= 0) & (keys < self.n)]
-            u, c = np.unique(keys, return_counts=True)
-            ok = (res[u] == 0) & ~self.inflight[u]
-            u, c = u[ok], c[ok]
-            want = u[np.argsort(-c, kind="stable")]
-        self.ring_seen = cnt
-        self.stats["masked"] += max(0, new)
+        if new <= 0:
+            return np.zeros(0, dtype=np.int64), 0
+        self.stats["masked"] += new
+        logged = ring[1 + np.arange(count - new, count) % self.cap].astype(np.int64)
+        keys, hits = np.unique(logged[(logged >= 0) & (logged < self.n)], return_counts=True)
+        absent = self.state[keys] == ABSENT
+        keys, hits = keys[absent], hits[absent]
+        return keys[np.lexsort((keys, -hits))], new
 
-        # budget
-        inflight_n = int(self.inflight.sum())
-        over = int(res.sum()) + inflight_n + len(want) - self.budget
-        dropped = np.zeros(0, dtype=np.int64)
-        if over > 0:
-            c1 = np.nonzero((res == 1) & vram & ~self.pinned)[0]
-            t1 = c1[np.argsort(self.age[c1], kind="stable")[:over]]
-            t2 = np.zeros(0, dtype=np.int64)
-            if over > len(t1):
-                m = (res == 1) & ~self.pinned & (self.age <= self.tick - self.min_age)
-                m[t1] = False
-                c2 = np.nonzero(m)[0]
-                t2 = c2[np.argsort(self.age[c2], kind="stable")[: over - len(t1)]]
-            dropped = np.concatenate([t1, t2]).astype(np.int64)
-            res[dropped] = 0
-            self.stats["dropped"] += len(dropped)
+    def _make_room(self, n_want: int, in_vram: np.ndarray) -> np.ndarray:
+        excess = int(np.count_nonzero(self.state != ABSENT)) + n_want - self.budget
+        if excess <= 0:
+            return np.zeros(0, dtype=np.int64)
+        droppable = (self.state == RESIDENT) & ~self.pinned & (in_vram | (self.since <= self.tick - self.min_age))
+        cand = np.flatnonzero(droppable)
+        drop = cand[np.lexsort((self.since[cand], ~in_vram[cand]))[:excess]]
+        self.state[drop] = ABSENT
+        self.stats["dropped"] += drop.size
+        return drop
 
-        # admission
-        free = self.budget - int(res.sum()) - inflight_n
+    def _admit(self, want: np.ndarray) -> None:
+        room = self.budget - int(np.count_nonzero(self.state != ABSENT))
         if self.max_inflight is not None:
-            free = min(free, self.max_inflight - inflight_n)
-        admit = want[: max(0, free)]
-        self.stats["admit_deferred"] += len(want) - len(admit)
-        for key in admit.tolist():
-            self.inflight[key] = True
+            room = min(room, self.max_inflight - int(np.count_nonzero(self.state == FETCHING)))
+        take = want[:max(0, room)]
+        self.stats["admit_deferred"] += len(want) - len(take)
+        for key in take.tolist():
+            self.state[key] = FETCHING
             self.stats["fetches"] += 1
             self.fetch(key)
 
-        # upload the changed flags; the dropped keys' release waits for their clear
-        diff = np.nonzero(res != res_d)[0].astype(np.int64)
-        if len(diff):
-            self._upload(diff, res[diff])
-            self._last_diff = (diff, res[diff].copy())
-        else:
-            self._last_diff = None
-        if len(dropped):
-            self._clears.append((self._event(), self.tick, dropped))
-        self.res = res
-        self.stats["steps"] += 1
-        return int(max(0, new))
-
-    def resident(self) -> int:
-        return int(self.res.sum())
+    def _write_flags(self, flags: np.ndarray) -> None:
+        mine = self.state == RESIDENT
+        keys = np.flatnonzero(mine != flags)
+        if not keys.size:
+            return
+        idx = torch.from_numpy(keys)
+        val = torch.from_numpy(mine[keys].astype(np.uint8))
+        if self.ram_res.is_cuda:
+            idx = idx.pin_memory().to(self.ram_res.device, non_blocking=True)
+            val = val.pin_memory().to(self.ram_res.device, non_blocking=True)
+        self.ram_res.index_copy_(0, idx, val)

@@ -98,6 +98,30 @@ def test_victim_writeback_becomes_resident_and_rescues_a_drop():
     assert t.res[6] == 1 and t.res[5] == 0  # 6 is resident again (youngest); 5 made room
 
 
+def test_a_dropped_key_fetched_again_keeps_its_host_copy():
+    """A key dropped and wanted again before its release point is being fetched into the same host copy: release()
+    must not free it."""
+    dev = FakeDevice()
+    t, fetched, released = _tier(dev, budget=2)
+    t.step()
+    for key in [1, 3]:                      # resident at steps 4 and 6
+        dev.log_misses([key])
+        t.step()
+        t.step()
+        t.fill_done(key)
+    t.step()
+    dev.log_misses([2])
+    t.step()
+    dev.log_misses([1])                     # logged before the drop below is read: it reaches the host one step later
+    t.step()                                # 2 wanted: 1 (oldest) dropped, 2 fetched
+    assert fetched[-1] == 2 and t.res[1] == 0
+    t.step()                                # 1 wanted again: 3 dropped, 1 fetched
+    assert fetched[-1] == 1
+    for _ in range(3):
+        t.step()
+    assert 1 not in released and released == [3] and t.stats["release_rescued"] == 1
+
+
 def test_pinned_keys_are_never_dropped():
     dev = FakeDevice()
     pinned = np.zeros(16, dtype=bool)
