@@ -41,6 +41,14 @@ __device__ __forceinline__ int block_scan(int v, int* total, int* sh_warp /* [32
     return base + x - v;
 }
 
+// LRU order key of slot s at tick T: 0 for an empty slot (slot_last -1), else its last use + 1.  A slot used at this
+// tick (slot_last >= T: a hit of this call, or pinned at 0x7FFFFFFF) is not eligible and has no key.
+__device__ __forceinline__ bool lru_key(int last, int T, uint32_t& key) {
+    if (last >= T) return false;
+    key = (uint32_t)(last + 1);
+    return true;
+}
+
 struct EnsureArgs {
     int32_t* ids; float* w; int npairs; int layer; int E; int S;
     int64_t* ptrs_all; int32_t* slot_of; int32_t* slot_key; int32_t* slot_last; int32_t* tick;
@@ -142,8 +150,8 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     const int s0 = tid * C, s1 = min(S, s0 + C);
     int elig = 0, empty = 0;
     for (int s = s0; s < s1; ++s) {
-        int la = a.slot_last[s];
-        if (la < T) { ++elig; empty += (la == -1); }
+        uint32_t k;
+        if (lru_key(a.slot_last[s], T, k)) { ++elig; empty += (k == 0); }
     }
     block_scan(elig, &total, sh_warp);
     int n_elig = total;
@@ -163,13 +171,12 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
         for (int shift = 24; shift >= 0; shift -= 8) {
             for (int b = tid; b < 256; b += kEnsureThreads) hist[b] = 0;
             __syncthreads();
-            uint32_t hmask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+            // histogram of byte `shift` over the eligible keys whose higher bytes equal the prefix found so far
+            const uint64_t high = (uint64_t)prefix >> (shift + 8);
             for (int s = s0; s < s1; ++s) {
-                int la = a.slot_last[s];
-                if (la >= T) continue;
-                uint32_t u = (uint32_t)(la + 1);
-                if ((u & hmask) != (prefix & hmask)) continue;
-                atomicAdd(&hist[(u >> shift) & 255], 1);
+                uint32_t k;
+                if (lru_key(a.slot_last[s], T, k) && ((uint64_t)k >> (shift + 8)) == high)
+                    atomicAdd(&hist[(k >> shift) & 255], 1);
             }
             __syncthreads();
             if (tid < 32) {
@@ -199,34 +206,25 @@ __device__ __forceinline__ void ensure_block(const EnsureArgs& a) {
     // 7. selection: every eligible u < tau plus the first `want` (ascending slot index) with u == tau
     int n_eq = 0;
     for (int s = s0; s < s1; ++s) {
-        int la = a.slot_last[s];
-        if (la < T && (uint32_t)(la + 1) == prefix) ++n_eq;
+        uint32_t k;
+        n_eq += lru_key(a.slot_last[s], T, k) && k == prefix;
     }
-    int eq_before = block_scan(n_eq, &total, sh_warp);
-    int nsel = 0;
-    {
+    const int eq_before = block_scan(n_eq, &total, sh_warp);
+    // this thread's chunk in slot order: calls take(s) for every selected slot (the keys equal to tau are numbered
+    // across the block from eq_before, and the first `want` of them are selected)
+    auto for_each_selected = [&](auto&& take) {
         int eq = eq_before;
         for (int s = s0; s < s1; ++s) {
-            int la = a.slot_last[s];
-            if (la >= T) continue;
-            uint32_t u = (uint32_t)(la + 1);
-            if (u < prefix) ++nsel;
-            else if (u == prefix) { if (eq < want) ++nsel; ++eq; }
+            uint32_t k;
+            if (!lru_key(a.slot_last[s], T, k) || k > prefix) continue;
+            if (k == prefix && eq++ >= want) continue;
+            take(s);
         }
-    }
-    int sel_before = block_scan(nsel, &total, sh_warp);
-    {
-        int eq = eq_before, r = sel_before;
-        for (int s = s0; s < s1; ++s) {
-            int la = a.slot_last[s];
-            if (la >= T) continue;
-            uint32_t u = (uint32_t)(la + 1);
-            bool take = false;
-            if (u < prefix) take = true;
-            else if (u == prefix) { take = eq < want; ++eq; }
-            if (take) { if (r < 1024) vslot[r] = s; ++r; }
-        }
-    }
+    };
+    int nsel = 0;
+    for_each_selected([&](int) { ++nsel; });
+    int r = block_scan(nsel, &total, sh_warp);
+    for_each_selected([&](int s) { if (r < 1024) vslot[r] = s; ++r; });
     if (tid == 0) sh_nm = total < nm ? total : nm;
     __syncthreads();
     nm = sh_nm;
