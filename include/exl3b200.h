@@ -74,6 +74,34 @@ int exl3b_victim_copy(const int32_t* vict, const int64_t* host_base, int64_t slo
 int exl3b_commit(const int32_t* fill_list, int64_t* ptrs, int64_t* fill, const int32_t* pf_slot, int64_t slot_base,
                  int64_t blob, void* stream);
 
+/* ---- copy-engine prefetch ------------------------------------------------------------------------------------ */
+/* Replaces moe_prefetch_plan (kernels/moe-a8/exl3_moe.a8.sycl:1127-1142), the plan mode of launch_ensure
+ * (:898-1036): commits landed plans (as exl3b_cepf_commit); then, unless this layer's previous plan is still in
+ * flight, claims up to max_fill (<= 16) LRU slots for the experts of ids that are not in VRAM, exactly as
+ * exl3b_ensure's prefetch mode does (tick not advanced), pins them (slot_last = INT_MAX), records them in pend
+ * (int32 [n_layers][35]: n, seq, T, (expert, slot) x 16) and publishes [seq, n, T, layer, (expert, slot) x n] to the
+ * layer's record of plans (pinned host memory, int32 [n_layers][4 + 2E]), seq written last behind a system-scope
+ * fence.  plan_seq: int32 [n_layers] device counters.  The table keeps pointing at the host copies until the commit. */
+int exl3b_cepf_plan(const int32_t* ids, int n, int layer, int E, int S, int64_t* ptrs_all, int32_t* slot_of,
+                    int32_t* slot_key, int32_t* slot_last, int32_t* tick, const int64_t* host_base, int64_t slot_base,
+                    int64_t blob, int64_t hstride, int32_t* pf_list, int32_t* pf_slot, int max_fill, int32_t* plans,
+                    int32_t* plan_seq, int32_t* pend, const int32_t* done_seq, int n_layers, void* stream);
+/* Replaces the pend / done_seq commit at the head of launch_ensure (:874-896): every layer whose done_seq (int32
+ * [n_layers], written by the worker's copy stream) reached its pending seq gets its planned ptrs_all entries pointed
+ * at their slots and the slots unpinned (slot_last = the plan's tick). */
+int exl3b_cepf_commit(int32_t* pend, const int32_t* done_seq, int n_layers, int E, int S, int64_t* ptrs_all,
+                      int32_t* slot_last, int64_t slot_base, int64_t blob, void* stream);
+/* Replaces moe_prefetch_worker_start / moe_prefetch_worker_stop (:1048-1124): one host thread per process that turns
+ * each newly published plan into cudaMemcpyAsync copies (host_base[layer] + expert * hstride -> slot) on copy_stream
+ * followed by a kernel writing done_seq[layer] = seq on the same stream.  host_base: host array of n_layers addresses.
+ * stop handles the plans already published, waits for copy_stream, writes counts[0] = plans, counts[1] = copies, and
+ * returns non-zero when a copy failed (that plan then stays in flight and its experts are read from host). */
+int exl3b_cepf_worker_start(const int32_t* plans, int n_layers, int E, int S, const int64_t* host_base,
+                            int64_t slot_base, int64_t blob, int64_t hstride, int32_t* done_seq, int device,
+                            void* copy_stream);
+int exl3b_cepf_worker_stop(int64_t* counts);
+int exl3b_cepf_worker_running(void);
+
 /* ---- routed MoE, decode (few tokens) ------------------------------------------------------------------------- */
 /* Replaces moe_forward_impl's GEMV path (exl3_moe.a8.sycl:1263-1314: GateUpKernel :121-260, DownKernel :264-368,
  * CombineKernel :371-395) for M tokens (any M; intended for M <= 64): out[m] = sum_k w[m,k] * expert(ids[m,k])(x[m]).

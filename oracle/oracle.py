@@ -308,3 +308,39 @@ class CacheState:
         lib().ora_commit(p, f, self.fill_list)
         self.ptrs_all[layer * E:(layer + 1) * E] = p
         self.fill_all[layer * E:(layer + 1) * E] = f
+
+    # ---- copy-engine prefetch: the plan and commit modes of launch_ensure (exl3_moe.a8.sycl:874-905, 898-1036)
+    PINNED = 0x7FFFFFFF
+
+    def cepf_reset(self) -> None:
+        self.pend = {}                                   # layer -> (seq, T, [(expert, slot), ...]) in flight
+        self.plan_seq = np.zeros(self.L, np.int32)
+
+    def cepf_commit(self, done_seq) -> None:
+        """Every layer whose done_seq reached its pending seq: table entries -> slots, slots unpinned (last = T)."""
+        for li in sorted(self.pend):
+            seq, T, pairs = self.pend[li]
+            if int(done_seq[li]) < seq:
+                continue
+            for e, s in pairs:
+                self.ptrs_all[li * self.E + e] = self.slot_base + s * self.blob
+                self.slot_last[s] = T
+            del self.pend[li]
+
+    def cepf_plan(self, ids: np.ndarray, layer: int, max_fill: int, done_seq):
+        """Commit what landed; a layer with a plan in flight plans nothing (returns None); else the prefetch-mode
+        cache step claims slots, which are pinned and recorded.  Returns (seq, [(expert, slot), ...])."""
+        self.cepf_commit(done_seq)
+        if layer in self.pend:
+            self.fill_list[0] = 0
+            return None
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+        n = self.ensure(ids, np.ones(ids.size, np.float32), layer, min(max_fill, 16, self.E), prefetch=True)
+        pairs = [(int(self.fill_list[1 + i]), int(self.pf_slot[i])) for i in range(n)]
+        for _, s in pairs:
+            self.slot_last[s] = self.PINNED
+        self.plan_seq[layer] += 1
+        seq = int(self.plan_seq[layer])
+        if pairs:
+            self.pend[layer] = (seq, int(self.tick[0]), pairs)
+        return seq, pairs

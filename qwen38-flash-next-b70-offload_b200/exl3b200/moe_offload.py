@@ -180,6 +180,7 @@ class ExpertStore:
         self._cache_used = False          # forward_cached / prefetch ran since the mirror was read
         self._stage = [None, None]        # prefill staging buffers [E, blob], allocated on first use
         self._staging: _Staging | None = None
+        self._cepf_stream = None          # the copy stream while copy-engine prefetch runs
         # device cache state, the arguments of moe_forward_cached / moe_prefetch: name -> (entries, dtype, initial)
         i32, i64 = torch.int32, torch.int64
         state = {"ptrs_all": (LE, i64, 0),           # blob address of every (layer, expert): host copy or slot
@@ -253,6 +254,7 @@ class ExpertStore:
         """Copy `experts` of `key` that are not in VRAM into free slots, then point the table and the device slot map
         at them, all ordered on `stream` (default: the current stream).  Returns the number copied
         (moe_offload.py:154-185)."""
+        self._no_copy_prefetch("make_resident")
         self._resync()
         li = self.layer_index[key]
         mine = self.slot_of[key]
@@ -285,6 +287,7 @@ class ExpertStore:
     def evict(self, key, experts) -> None:
         """Point `experts` of `key` back at their host copies; a freed slot is refilled only after the work queued on
         the current stream so far (moe_offload.py:187-216)."""
+        self._no_copy_prefetch("evict")
         self._resync()
         li = self.layer_index[key]
         mine = self.slot_of[key]
@@ -355,12 +358,71 @@ class ExpertStore:
                             self.slot_last, self.tick, self.host_base, self.slot_base, self.pf_list, self.pf_slot,
                             max_fill, self.E, self.blob)
 
+    # ---- copy-engine prefetch
+    def _no_copy_prefetch(self, what: str) -> None:
+        if self._cepf_stream is not None:
+            raise RuntimeError(f"ExpertStore.{what}: stop_copy_prefetch first (planned slots may still be filling)")
+
+    def start_copy_prefetch(self) -> None:
+        """Start the host worker that turns device-written prefetch plans into copy-engine copies on a stream of its
+        own (moe_offload.py:264-280).  While it runs, plan_prefetch publishes plans and every cached MoE call first
+        commits the plans that have landed; static placement and staged prefill wait for stop_copy_prefetch."""
+        if self._cepf_stream is not None:
+            raise RuntimeError("ExpertStore: copy prefetch is already running")
+        L, E = len(self.layer_index), self.E
+        if not L or not self.n_slots:
+            raise RuntimeError("ExpertStore: copy prefetch needs layers and slots")
+        self._plans = self.X.host_alloc(L * (4 + 2 * E) * 4)
+        self._plans.zero_()
+        self._plan_seq = torch.zeros(L, dtype=torch.int32, device=self.dev)
+        self.done_seq = torch.zeros(L, dtype=torch.int32, device=self.dev)
+        self.pend.zero_()
+        bases = torch.zeros(L, dtype=torch.int64)
+        for key, li in self.layer_index.items():
+            bases[li] = int(self._host_ptr[key][0])
+        torch.cuda.synchronize(self.dev)
+        stream = torch.cuda.Stream(self.dev)
+        with torch.cuda.stream(stream):
+            self.X.moe_prefetch_worker_start(self._plans, bases, self.slot_base, self.blob, self.ptrs_all,
+                                             self.slot_last, torch.empty(0, dtype=torch.uint8), self.done_seq, L, E)
+        self._cepf_stream = stream
+
+    def plan_prefetch(self, key, ids: torch.Tensor, max_fill: int = 16) -> None:
+        """On the COMPUTE stream (e.g. right after one layer's MoE call, for the next layer): claim and pin LRU slots
+        for the predicted experts `ids` of `key` (at most 16) and publish the plan; the worker copies them on the copy
+        engine and a later cached call commits them.  The compute stream never waits (moe_offload.py:282-289)."""
+        if self._cepf_stream is None:
+            raise RuntimeError("ExpertStore: start_copy_prefetch first")
+        ids = _as_route(ids, torch.int32)
+        self._cache_used = True
+        self.X.moe_prefetch_plan(ids.flatten(), self.ptrs_all, self.layer_index[key], self.slot_of_dev, self.slot_key,
+                                 self.slot_last, self.tick, self.host_base, self.slot_base, self.pf_list, self.pf_slot,
+                                 self._plans, self._plan_seq, self.pend, self.done_seq, max_fill, self.E, self.blob)
+
+    def stop_copy_prefetch(self) -> list:
+        """Stop the worker once it has copied every plan queued so far and commit them; returns [plans handled,
+        experts copied] (moe_offload.py:291-302).  Afterwards cached calls run without prefetch commits."""
+        if self._cepf_stream is None:
+            return [0, 0]
+        cs = torch.cuda.current_stream(self.dev)
+        cs.synchronize()                                   # every queued plan has been published
+        try:
+            counts = self.X.moe_prefetch_worker_stop()     # copies them and waits for the copy stream
+        finally:
+            _ops.cepf_commit(self.pend, self.done_seq, self.E, self.ptrs_all, self.slot_last, self.slot_base,
+                             self.blob)
+            cs.synchronize()
+            self.done_seq = torch.zeros(0, dtype=torch.int32, device=self.dev)
+            self._cepf_stream = None
+        return counts
+
     # ---- prefill staging
     def stage_layer(self, key, buf: int, stream) -> torch.Tensor:
         """Queue on `stream` the copy of every expert of `key` that is not in VRAM into staging buffer `buf` (0 or 1),
         runs of consecutive experts as one copy; returns the layer's pointer table for forward(ptrs=...), valid once
         `stream` has been waited on: slots for resident experts, the staging buffer for the rest
         (moe_offload.py:305-329)."""
+        self._no_copy_prefetch("stage_layer")
         if self._stage[buf] is None:
             self._stage[buf] = torch.empty((self.E, self.blob), dtype=torch.uint8, device=self.dev)
         base = s64(self._stage[buf].data_ptr())
@@ -381,6 +443,7 @@ class ExpertStore:
 
     def reset_cache(self) -> None:
         """Empty every slot and point every table at host memory (waits for the current stream's queued work)."""
+        self._no_copy_prefetch("reset_cache")
         cs = _current(self.dev)
         if cs is not None:
             cs.synchronize()

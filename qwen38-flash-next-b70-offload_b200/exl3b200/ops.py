@@ -219,14 +219,14 @@ def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot
     E = n_experts
     M = x.shape[0]
     ptrs_l = ptrs_all.narrow(0, layer * E, E)
+    if pend.numel() and done_seq.numel():   # copy-engine prefetch on: commit the plans that have landed first
+        cepf_commit(pend, done_seq, E, ptrs_all, slot_last, slot_base, blob_bytes(x.shape[1], I, K))
     if M == 0 or M >= G.prefill_min_m or slot_key.numel() == 0:
         y = _moe_forward_impl(x, topk_ids, topk_w, ptrs_l, I, K, E)
         if out is not None:
             out.copy_(y)
             return out
         return y
-    if pend.numel() and done_seq.numel():
-        raise RuntimeError("exl3b200 moe_forward_cached: copy-engine prefetch commits (pend/done_seq) not available")
     _check_route(topk_ids, topk_w)
     _check_x(x)
     H = x.shape[1]
@@ -272,6 +272,71 @@ def _moe_prefetch_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick,
                                 s), "prefetch copy")
     check(L.exl3b_commit(pf_list.data_ptr(), ptrs_l.data_ptr(), None, pf_slot.data_ptr(), slot_base, blob, s),
           "prefetch commit")
+
+
+# ------------------------------------------------------------------------------------------------ copy-engine prefetch
+_PEND_STRIDE = 35     # int32 per layer in pend: n, seq, T, (expert, slot) x 16
+_PLAN_MAX = 16
+
+
+def cepf_commit(pend, done_seq, n_experts, ptrs_all, slot_last, slot_base, blob) -> None:
+    """Commit every landed copy-engine plan (exl3b_cepf_commit) on the current stream."""
+    check(_lib.lib().exl3b_cepf_commit(pend.data_ptr(), done_seq.data_ptr(), done_seq.numel(), n_experts,
+                                       slot_last.numel(), ptrs_all.data_ptr(), slot_last.data_ptr(), slot_base, blob,
+                                       stream(ptrs_all.device)), "copy prefetch commit")
+
+
+def _moe_prefetch_plan_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base, slot_base, pf_list,
+                            pf_slot, plans, plan_seq, pend, done_seq, max_fill, n_experts, blob):
+    """moe_prefetch_plan (exl3_moe.a8.sycl:1127-1142): claim and pin LRU slots for the predicted experts of `layer`
+    and publish the plan to the pinned host buffer `plans` for the copy worker (exl3b_cepf_plan)."""
+    if ids.dtype != torch.int32 or not ids.is_contiguous():
+        raise RuntimeError("exl3b200 moe_prefetch_plan: contiguous int32 ids")
+    E, S, n_layers = n_experts, slot_key.numel(), done_seq.numel()
+    if S == 0 or ids.numel() == 0:
+        return
+    if plans.device.type != "cpu" or not plans.is_pinned() or plans.numel() * plans.element_size() < \
+            n_layers * (4 + 2 * E) * 4:
+        raise RuntimeError("exl3b200 moe_prefetch_plan: plans must be pinned host memory of n_layers x (4 + 2E) int32")
+    if pend.numel() < n_layers * _PEND_STRIDE or plan_seq.numel() < n_layers:
+        raise RuntimeError("exl3b200 moe_prefetch_plan: pend needs 35 int32 and plan_seq one per layer")
+    mf = min(max_fill, _PLAN_MAX, pf_slot.numel())
+    check(_lib.lib().exl3b_cepf_plan(ids.data_ptr(), ids.numel(), layer, E, S, ptrs_all.data_ptr(), slot_of.data_ptr(),
+                                     slot_key.data_ptr(), slot_last.data_ptr(), tick.data_ptr(), host_base.data_ptr(),
+                                     slot_base, blob, G.host_stride or blob, pf_list.data_ptr(), pf_slot.data_ptr(), mf,
+                                     plans.data_ptr(), plan_seq.data_ptr(), pend.data_ptr(), done_seq.data_ptr(),
+                                     n_layers, stream(ids.device)), "moe_prefetch_plan")
+
+
+_worker_atexit = False
+
+
+def moe_prefetch_worker_start(plans, host_base_cpu, slot_base, blob, ptrs_all, slot_last, commit_host, done_seq,
+                              n_layers, n_experts) -> None:
+    """moe_prefetch_worker_start (exl3_moe.a8.sycl:1092-1115): start the host thread that turns published plans into
+    copy-engine copies on the CURRENT stream (call it inside `with torch.cuda.stream(copy_stream)`).  commit_host is
+    accepted for the reference's signature; this worker needs no host commit buffer."""
+    global _worker_atexit
+    hb = host_base_cpu.to(torch.int64).contiguous()
+    if hb.numel() < n_layers:
+        raise RuntimeError("exl3b200 moe_prefetch_worker_start: host_base_cpu needs one address per layer")
+    dev = done_seq.device
+    check(_lib.lib().exl3b_cepf_worker_start(plans.data_ptr(), n_layers, n_experts, slot_last.numel(), hb.data_ptr(),
+                                             slot_base, blob, G.host_stride or blob, done_seq.data_ptr(), dev.index,
+                                             stream(dev)), "moe_prefetch_worker_start")
+    if not _worker_atexit:   # a worker still running at interpreter exit would read freed host memory
+        import atexit
+        atexit.register(lambda: _lib.lib().exl3b_cepf_worker_stop(None))
+        _worker_atexit = True
+
+
+def moe_prefetch_worker_stop() -> list:
+    """moe_prefetch_worker_stop (:1117-1124): handle the plans already published, wait for the copies, stop; returns
+    [plans handled, experts copied]."""
+    import ctypes
+    counts = (ctypes.c_int64 * 2)()
+    check(_lib.lib().exl3b_cepf_worker_stop(counts), "moe_prefetch_worker_stop")
+    return [int(counts[0]), int(counts[1])]
 
 
 def align(topk_ids: torch.Tensor, topk_w: torch.Tensor, n_experts: int, pad: int):
@@ -393,6 +458,10 @@ def register() -> None:
     lib.define("moe_prefetch(Tensor ids, Tensor(a!) ptrs_all, int layer, Tensor(b!) slot_of, Tensor(c!) slot_key, "
                "Tensor(d!) slot_last, Tensor tick, Tensor host_base, int slot_base, Tensor(e!) pf_list, "
                "Tensor(f!) pf_slot, int max_fill, int n_experts, int blob) -> ()")
+    lib.define("moe_prefetch_plan(Tensor ids, Tensor(a!) ptrs_all, int layer, Tensor(b!) slot_of, Tensor(c!) slot_key, "
+               "Tensor(d!) slot_last, Tensor tick, Tensor host_base, int slot_base, Tensor(e!) pf_list, "
+               "Tensor(f!) pf_slot, Tensor(g!) plans, Tensor(h!) plan_seq, Tensor(i!) pend, Tensor done_seq, "
+               "int max_fill, int n_experts, int blob) -> ()")
     lib.define("moe_align(Tensor topk_ids, Tensor topk_w, int n_experts, int pad) -> Tensor[]")
     lib.define("router_topk(Tensor x, Tensor wr, Tensor? bias, int topk) -> (Tensor, Tensor)")
     lib.define("moe_forward_mixed(Tensor x, Tensor topk_ids, Tensor topk_w, Tensor ptrs, Tensor kinfo, int I, "
@@ -400,6 +469,7 @@ def register() -> None:
     lib.impl("moe_forward", _moe_forward_impl, "CUDA")
     lib.impl("moe_forward_cached", _moe_forward_cached_impl, "CUDA")
     lib.impl("moe_prefetch", _moe_prefetch_impl, "CUDA")
+    lib.impl("moe_prefetch_plan", _moe_prefetch_plan_impl, "CUDA")
     lib.impl("moe_align", _moe_align_impl, "CUDA")
     lib.impl("router_topk", lambda x, wr, bias, topk: router_topk(x, wr, bias, topk), "CUDA")
     lib.impl("moe_forward_mixed", _moe_forward_mixed_impl, "CUDA")
@@ -421,15 +491,16 @@ class _Ops:
     def __getattr__(self, name):
         register()
         if hasattr(torch.ops.exl3b200_moe, name) and name in ("moe_forward", "moe_forward_cached", "moe_prefetch",
-                                                               "moe_align", "router_topk", "moe_forward_mixed",
-                                                               "moe_forward_shared"):
+                                                               "moe_prefetch_plan", "moe_align", "router_topk",
+                                                               "moe_forward_mixed", "moe_forward_shared"):
             return getattr(torch.ops.exl3b200_moe, name)
         fn = {"host_alloc": host_alloc, "usm_kind": usm_kind, "memcpy_async": memcpy_async,
               "blob_bytes": blob_bytes, "moe_set_splits": moe_set_splits, "moe_set_mr": moe_set_mr,
               "moe_set_debug": moe_set_debug, "moe_set_pair_max_m": moe_set_pair_max_m,
               "moe_set_prefill_min_m": moe_set_prefill_min_m, "moe_set_victims": moe_set_victims,
               "moe_set_tier": moe_set_tier, "moe_set_host_stride": moe_set_host_stride,
-              "moe_svm_prefetch": moe_svm_prefetch}.get(name)
+              "moe_svm_prefetch": moe_svm_prefetch, "moe_prefetch_worker_start": moe_prefetch_worker_start,
+              "moe_prefetch_worker_stop": moe_prefetch_worker_stop}.get(name)
         if fn is None:
             raise AttributeError(name)
         return fn

@@ -53,11 +53,26 @@ def test_blob_bytes_and_abi():
                                  1 << 20, 2048, 1, 1 << 20, 16, 1, None),          # workspace too small
     lambda L: L.exl3b_router_topk(1 << 20, 2048, 1 << 20, None, 1, 2048, 512, 40, 1 << 20, 1 << 20, 1 << 20, None, None),
     lambda L: L.exl3b_align(1 << 20, 1 << 20, 10, 10, 512, 32, 1 << 20, 1 << 20, 9, 10, 1 << 20, 1 << 20, None),
+    lambda L: L.exl3b_cepf_plan(*([1 << 20, 4, 0, 512, 8] + [1 << 20] * 6 + [0, 64, 64, 1 << 20, 1 << 20, 17] +
+                                  [1 << 20] * 4 + [1, None])),                      # max_fill > 16
+    lambda L: L.exl3b_cepf_plan(*([1 << 20, 4, 3, 512, 8] + [1 << 20] * 6 + [0, 64, 64, 1 << 20, 1 << 20, 8] +
+                                  [1 << 20] * 4 + [2, None])),                      # layer outside the plan buffer
+    lambda L: L.exl3b_cepf_commit(None, 1 << 20, 2, 512, 8, 1 << 20, 1 << 20, 0, 64, None),
+    lambda L: L.exl3b_cepf_worker_start(1 << 20, 0, 512, 8, 1 << 20, 0, 64, 64, 1 << 20, 0, None),   # no layers
 ])
 def test_invalid_arguments_rejected_before_launch(call):
     L = _lib.lib()
     assert call(L) == 1
     assert L.exl3b_last_error()
+
+
+def test_copy_prefetch_worker_idle():
+    """No worker running: stop is a no-op that reports zero plans and copies."""
+    import ctypes
+    L = _lib.lib()
+    counts = (ctypes.c_int64 * 2)(7, 7)
+    assert L.exl3b_cepf_worker_running() == 0
+    assert L.exl3b_cepf_worker_stop(counts) == 0 and list(counts) == [0, 0]
 
 
 def test_missing_library_fails_loudly(tmp_path, monkeypatch):

@@ -238,3 +238,19 @@ def test_pack_expert_into_buffer_checks_size():
     with pytest.raises(ValueError):
         moe_offload.pack_expert(gate, up, down, 3, out=torch.zeros(blob.numel() + 1, dtype=torch.uint8))
     assert np.array_equal(blob[-64 * 2:].numpy(), torch.ones(64, dtype=torch.float16).view(torch.uint8).numpy())
+
+
+def test_copy_prefetch_guards(fake):
+    """While the copy-engine prefetch worker runs, static placement and staged prefill are refused (their tables
+    could point at a slot whose copy has not landed); planning needs a running worker."""
+    st, keys = _store()
+    with pytest.raises(RuntimeError, match="start_copy_prefetch first"):
+        st.plan_prefetch(keys[0], torch.tensor([1], dtype=torch.int32))
+    assert st.stop_copy_prefetch() == [0, 0]              # not running: nothing to stop
+    st._cepf_stream = object()                             # as start_copy_prefetch leaves it
+    for call in (lambda: st.make_resident(keys[0], [1]), lambda: st.evict(keys[0], [1]), st.reset_cache,
+                 lambda: st.stage_layer(keys[0], 0, None),
+                 lambda: st.forward_prefill_staged(keys[0], torch.zeros(1, 64), torch.zeros(1, 1, dtype=torch.int32),
+                                                   torch.ones(1, 1))):
+        with pytest.raises(RuntimeError, match="stop_copy_prefetch first"):
+            call()
