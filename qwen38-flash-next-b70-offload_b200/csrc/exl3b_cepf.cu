@@ -123,10 +123,15 @@ struct CepfWorker {
             if (seq == seen[li]) continue;
             seen[li] = seq;
             any = true;
-            const int n = __atomic_load_n(rec + 1, __ATOMIC_RELAXED);
+            // the device writes the pairs, then n, then seq, each behind a system-scope fence; a record is rewritten
+            // only after its plan committed (which needs this worker's done write), so reading n and then the pairs
+            // in order sees one plan: at worst a newer one under an older seq, whose copies are right and whose done
+            // value (the older seq) commits nothing
+            const int n = __atomic_load_n(rec + 1, __ATOMIC_ACQUIRE);
             bool ok = n >= 0 && n <= kPendMax;
             for (int i = 0; ok && i < n; ++i) {
-                const int e = rec[4 + 2 * i], s = rec[5 + 2 * i];
+                const int e = __atomic_load_n(rec + 4 + 2 * i, __ATOMIC_RELAXED);
+                const int s = __atomic_load_n(rec + 5 + 2 * i, __ATOMIC_RELAXED);
                 if (e < 0 || e >= E || s < 0 || s >= S) { ok = false; break; }
                 ok = cudaMemcpyAsync(reinterpret_cast<void*>(slot_base + (int64_t)s * blob),
                                      reinterpret_cast<const void*>(host_base[li] + (int64_t)e * hstride), (size_t)blob,
