@@ -242,9 +242,9 @@ class ExpertStore:
         return [None if c < 0 else (by_row[int(c) // self.E], int(c) % self.E) for c in self._mirror_key]
 
     def _to_dev(self, values, dtype: torch.dtype) -> torch.Tensor:
-        """A small index/value list on the device, copied from pinned memory without a host sync; the copy is
-        ordered on the current stream (the pinned buffer is kept until it has run)."""
-        t = torch.tensor(values, dtype=dtype)
+        """A small index/value list (or CPU tensor) on the device, copied from pinned memory without a host sync; the
+        copy is ordered on the current stream (the pinned buffer is kept until it has run)."""
+        t = values.to(dtype) if isinstance(values, torch.Tensor) else torch.tensor(values, dtype=dtype)
         if self.dev.type != "cuda":
             return t
         return t.pin_memory().to(self.dev, non_blocking=True)
@@ -298,7 +298,7 @@ class ExpertStore:
         freed = mine[gone].tolist()
         at = self._to_dev([li * self.E + e for e in gone], torch.int64)
         sl = self._to_dev(freed, torch.int64)
-        self.ptrs_all.index_copy_(0, at, self._to_dev(self._host_ptr[key][gone].tolist(), torch.int64))
+        self.ptrs_all.index_copy_(0, at, self._to_dev(self._host_ptr[key][gone], torch.int64))
         self.slot_of_dev.index_fill_(0, at, -1)
         self.slot_key.index_fill_(0, sl, -1)
         self.slot_last.index_fill_(0, sl, -1)
@@ -439,7 +439,7 @@ class ExpertStore:
         table = torch.arange(self.E, dtype=torch.int64).mul_(self.blob).add_(base)
         held = mine >= 0
         table[held] = mine[held].to(torch.int64) * self.blob + self.slot_base
-        return self._to_dev(table.tolist(), torch.int64)
+        return self._to_dev(table, torch.int64)
 
     def reset_cache(self) -> None:
         """Empty every slot and point every table at host memory (waits for the current stream's queued work)."""

@@ -353,11 +353,9 @@ def align(topk_ids: torch.Tensor, topk_w: torch.Tensor, n_experts: int, pad: int
     ib = torch.empty(4 * A + 1 + 2 * P + 16 + mxb + 1, dtype=torch.int32, device=dev)
     fb = torch.empty(max(P, 1), dtype=torch.float32, device=dev)
     L = _lib.lib()
-    nblk = (P + 1023) // 1024
     scratch = torch.empty(max(int(L.exl3b_align_scratch(P, E)), 256), dtype=torch.uint8, device=dev)
     check(L.exl3b_align(topk_ids.data_ptr(), topk_w.data_ptr(), P, topk, E, pad, ib.data_ptr(), fb.data_ptr(), A, mxb,
                         scratch.data_ptr(), scratch.numel(), stream(dev)), "align")
-    del nblk
     return ib, fb
 
 
@@ -377,17 +375,34 @@ def usm_kind(p: int) -> int:
     return _usm_kind_cudart(p)
 
 
+_cudart_handle = None
+
+
+def _cudart():
+    """The CUDA runtime torch already loaded (same soname), with the two entry points used here typed once."""
+    global _cudart_handle
+    if _cudart_handle is None:
+        import ctypes
+        try:
+            rt = ctypes.CDLL("libcudart.so.12")
+        except OSError:
+            rt = ctypes.CDLL("libcudart.so")
+        rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                       ctypes.c_void_p]
+        rt.cudaMemcpyAsync.restype = ctypes.c_int
+        rt.cudaPointerGetAttributes.restype = ctypes.c_int
+        _cudart_handle = rt
+    return _cudart_handle
+
+
 def _usm_kind_cudart(p: int) -> int:
     import ctypes
-    try:
-        rt = ctypes.CDLL("libcudart.so.12")
-    except OSError:
-        rt = ctypes.CDLL("libcudart.so")
 
     class Attr(ctypes.Structure):
         _fields_ = [("type", ctypes.c_int), ("device", ctypes.c_int), ("devicePointer", ctypes.c_void_p),
                     ("hostPointer", ctypes.c_void_p)]
 
+    rt = _cudart()
     a = Attr()
     if rt.cudaPointerGetAttributes(ctypes.byref(a), ctypes.c_void_p(p)) != 0:
         rt.cudaGetLastError()
@@ -396,15 +411,9 @@ def _usm_kind_cudart(p: int) -> int:
 
 
 def memcpy_async(dst: int, src: int, nbytes: int) -> None:
-    """Async raw copy on the current stream (memcpy_async, exl3_moe.a8.sycl:1546-1549)."""
-    import ctypes
-    try:
-        rt = ctypes.CDLL("libcudart.so.12")
-    except OSError:
-        rt = ctypes.CDLL("libcudart.so")
-    rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
-    rc = rt.cudaMemcpyAsync(ctypes.c_void_p(dst), ctypes.c_void_p(src), ctypes.c_size_t(nbytes), 4,
-                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    """Async raw copy on the current stream (memcpy_async, exl3_moe.a8.sycl:1546-1549); cudaMemcpyDefault, so any
+    pair of host (pinned) and device addresses."""
+    rc = _cudart().cudaMemcpyAsync(dst, src, nbytes, 4, torch.cuda.current_stream().cuda_stream)
     if rc != 0:
         raise RuntimeError(f"exl3b200 memcpy_async: cudaMemcpyAsync failed ({rc})")
 
