@@ -13,7 +13,10 @@
  *   - the codebook range bound kQ8WMax = 3.453125 (experimental/n111-victim-ring/csrc/exl3_ops.sycl:522-525);
  *   - the blob sizes the reference asserts: 1,862,400 B at (H, I, K) = (2560, 640, 3)
  *     (kernels/moe-a8/exl3_moe.a8.sycl:7, experimental/n111-victim-ring/n111_test.py:21-23);
- *   - the cached-path == uncached-path identity (experimental/n111-victim-ring/n111_test.py:207-211).
+ *   - the cached-path == uncached-path identity (experimental/n111-victim-ring/n111_test.py:207-211);
+ *   - the blob bytes of the reference's own packer (plugin/exl3xpu/moe_offload.py:68-89, pure torch, run
+ *     on the CPU by tests/golden/make_ref_pack.py into tests/golden/ref_pack.npz): this restatement reads
+ *     those blobs back to the checkpoint words it was given (tests/test_oracle_codec.py).
  * Layer outputs (floating point) are therefore compared within the north-star tolerance.
  *
  * Every function cites the reference file:line it restates.  Arithmetic is kept in the same

@@ -6,7 +6,7 @@ The reference (SYCL/ESIMD for an Intel GPU) cannot run here and commits no golde
 fixtures are the oracle's own outputs on seeded synthetic inputs (exl3b200.synth, hash-based, identical on CPU and
 GPU).  They pin the oracle against accidental change and give the GPU tests a reference that needs no recomputation.
 What pins the oracle to the REFERENCE is listed in oracle/exl3b_oracle.c (codebook cross-statements, range bound,
-blob sizes) and checked by tests/test_oracle_codec.py.
+blob sizes, blobs packed by the reference's own packer) and checked by tests/test_oracle_codec.py.
 """
 from __future__ import annotations
 
