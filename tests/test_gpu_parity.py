@@ -368,6 +368,57 @@ def test_tier_mask_ring_and_safe(T, topk):
                        torch.zeros(0, dtype=torch.int32))
 
 
+def test_victim_write_back_restores_dropped_host_copies():
+    """Victim write-back (VictimCopyKernel, exl3_moe.a8.sycl:1168-1189, with the RAM-flag rule of the victim list
+    :1010-1018): an evicted slot whose expert the RAM tier no longer holds is copied back to the expert's host
+    address and flagged resident again; a victim the tier still holds is skipped (-1 in the list)."""
+    H, I, K, E, S, L = 256, 128, 3, 16, 4, 1
+    st = _store(H, I, K, E, S, L, seed=23)
+    key = list(st.layer_index)[0]
+    blobs = st.host[key].clone()
+    gold = torch.tensor(st._host_ptr[key].tolist(), dtype=torch.int64, device=DEV)
+    ram_res = torch.zeros(L * E, dtype=torch.uint8, device=DEV)
+    ram_res[:8] = 1
+    ring = torch.zeros(1 + 8, dtype=torch.int32, device=DEV)
+    safe = torch.zeros(L, dtype=torch.int32, device=DEV)
+    vict = torch.zeros(1 + 2 * E, dtype=torch.int32, device=DEV)
+    X.moe_set_tier(ram_res, ring, safe)
+    X.moe_set_victims(vict)
+    try:
+        cs = _oracle_state(st)
+        rr, rg, sf = ram_res.cpu().numpy(), ring.cpu().numpy(), safe.cpu().numpy()
+        vo = np.zeros(1 + 2 * E, np.int32)
+
+        def step(picks, seed):
+            x = synth.activations(1, H, seed).to(DEV)
+            ids = torch.tensor([picks], dtype=torch.int32)
+            w = torch.full((1, len(picks)), 1.0 / len(picks))
+            y = st.forward_cached(key, x, ids.to(DEV), w.to(DEV))
+            yr = X.moe_decode(x, ids.to(DEV), w.to(DEV), gold, I, K, E)
+            torch.cuda.synchronize()
+            assert torch.equal(y, yr), picks
+            cs.ensure(ids.numpy().copy(), w.numpy().copy(), 0, max_fill=E, ram_res=rr, ring=rg, safe=sf, vict=vo)
+            cs.commit(0)
+            _assert_state(st, cs)
+            assert np.array_equal(vict.cpu().numpy()[:1 + 2 * len(picks)], vo[:1 + 2 * len(picks)])
+
+        step([0, 1, 2, 3], 61)                     # four fills into empty slots: no write-back
+        ram_res[[0, 1]] = 0                        # the RAM tier drops experts 0 and 1 while they sit in VRAM
+        rr[[0, 1]] = 0
+        st.host[key][0].zero_()
+        st.host[key][1].zero_()
+        torch.cuda.synchronize()
+        step([4, 5, 6, 7], 62)                     # all four slots evicted
+        v = vict.cpu().numpy()
+        assert int(v[0]) == 4 and sorted(int(v[1 + 2 * i]) for i in range(4)) == [-1, -1, 0, 1]
+        assert torch.equal(st.host[key][0], blobs[0]) and torch.equal(st.host[key][1], blobs[1])
+        assert ram_res[:4].tolist() == [1, 1, 1, 1]
+    finally:
+        X.moe_set_victims(torch.zeros(0, dtype=torch.int32))
+        X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32),
+                       torch.zeros(0, dtype=torch.int32))
+
+
 def test_tier_host_loop_admits_missed_experts():
     """The RAM tier's host loop (exl3b200.tier.TierHost) against the decode kernels: picks in neither VRAM nor RAM
     are masked and logged; the loop fetches them (host copies are always valid here, so fetch completes at once) and
