@@ -384,7 +384,8 @@ class ExpertStore:
         stream = torch.cuda.Stream(self.dev)
         with torch.cuda.stream(stream):
             self.X.moe_prefetch_worker_start(self._plans, bases, self.slot_base, self.blob, self.ptrs_all,
-                                             self.slot_last, torch.empty(0, dtype=torch.uint8), self.done_seq, L, E)
+                                             self.slot_last, torch.empty(0, dtype=torch.uint8), self.done_seq, L, E,
+                                             keep=self)
         self._cepf_stream = stream
 
     def plan_prefetch(self, key, ids: torch.Tensor, max_fill: int = 16) -> None:

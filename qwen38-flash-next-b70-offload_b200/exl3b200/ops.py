@@ -309,14 +309,17 @@ def _moe_prefetch_plan_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, 
 
 
 _worker_atexit = False
+_worker_keep = None   # what the running worker reads or writes through raw addresses, alive until it stops
 
 
 def moe_prefetch_worker_start(plans, host_base_cpu, slot_base, blob, ptrs_all, slot_last, commit_host, done_seq,
-                              n_layers, n_experts) -> None:
+                              n_layers, n_experts, keep=None) -> None:
     """moe_prefetch_worker_start (exl3_moe.a8.sycl:1092-1115): start the host thread that turns published plans into
     copy-engine copies on the CURRENT stream (call it inside `with torch.cuda.stream(copy_stream)`).  commit_host is
-    accepted for the reference's signature; this worker needs no host commit buffer."""
-    global _worker_atexit
+    accepted for the reference's signature; this worker needs no host commit buffer.  The worker uses the plan
+    buffer, done_seq and the slot arena by address, so they are kept alive here until the stop, together with `keep`
+    (this build's extension: the owner of the slot arena and host arenas, e.g. the ExpertStore)."""
+    global _worker_atexit, _worker_keep
     hb = host_base_cpu.to(torch.int64).contiguous()
     if hb.numel() < n_layers:
         raise RuntimeError("exl3b200 moe_prefetch_worker_start: host_base_cpu needs one address per layer")
@@ -324,6 +327,7 @@ def moe_prefetch_worker_start(plans, host_base_cpu, slot_base, blob, ptrs_all, s
     check(_lib.lib().exl3b_cepf_worker_start(plans.data_ptr(), n_layers, n_experts, slot_last.numel(), hb.data_ptr(),
                                              slot_base, blob, G.host_stride or blob, done_seq.data_ptr(), dev.index,
                                              stream(dev)), "moe_prefetch_worker_start")
+    _worker_keep = (plans, done_seq, ptrs_all, slot_last, keep)
     if not _worker_atexit:   # a worker still running at interpreter exit would read freed host memory
         import atexit
         atexit.register(lambda: _lib.lib().exl3b_cepf_worker_stop(None))
@@ -333,9 +337,13 @@ def moe_prefetch_worker_start(plans, host_base_cpu, slot_base, blob, ptrs_all, s
 def moe_prefetch_worker_stop() -> list:
     """moe_prefetch_worker_stop (:1117-1124): handle the plans already published, wait for the copies, stop; returns
     [plans handled, experts copied]."""
+    global _worker_keep
     import ctypes
     counts = (ctypes.c_int64 * 2)()
-    check(_lib.lib().exl3b_cepf_worker_stop(counts), "moe_prefetch_worker_stop")
+    try:
+        check(_lib.lib().exl3b_cepf_worker_stop(counts), "moe_prefetch_worker_stop")
+    finally:
+        _worker_keep = None   # the worker has exited (stop joins it, also when it reports an error)
     return [int(counts[0]), int(counts[1])]
 
 

@@ -254,3 +254,38 @@ def test_copy_prefetch_guards(fake):
                                                    torch.ones(1, 1))):
         with pytest.raises(RuntimeError, match="stop_copy_prefetch first"):
             call()
+
+
+def test_copy_prefetch_worker_buffers_live_until_stop(monkeypatch):
+    """The worker reads the plan buffer and writes the slot arena by address: the op layer keeps them (and the
+    owner passed as `keep`) referenced until the stop, also when the stop reports a failed copy."""
+    from exl3b200 import ops
+
+    class FakeLib:
+        def __init__(self, rc):
+            self.rc = rc
+
+        def exl3b_cepf_worker_start(self, *args):
+            return 0
+
+        def exl3b_cepf_worker_stop(self, counts):
+            counts[0], counts[1] = 2, 5
+            return self.rc
+
+        def exl3b_last_error(self):
+            return b"a copy failed"
+
+    monkeypatch.setattr(ops, "stream", lambda dev=None: 0)
+    for rc in (0, 2):
+        monkeypatch.setattr(ops._lib, "lib", lambda rc=rc: FakeLib(rc))
+        owner, plans, done = object(), torch.zeros(64, dtype=torch.uint8), torch.zeros(2, dtype=torch.int32)
+        ops.moe_prefetch_worker_start(plans, torch.zeros(2, dtype=torch.int64), 0, 4096,
+                                      torch.zeros(8, dtype=torch.int64), torch.zeros(4, dtype=torch.int32),
+                                      torch.empty(0, dtype=torch.uint8), done, 2, 4, keep=owner)
+        assert ops._worker_keep[0] is plans and ops._worker_keep[1] is done and ops._worker_keep[-1] is owner
+        if rc == 0:
+            assert ops.moe_prefetch_worker_stop() == [2, 5]
+        else:
+            with pytest.raises(RuntimeError, match="a copy failed"):
+                ops.moe_prefetch_worker_stop()
+        assert ops._worker_keep is None
