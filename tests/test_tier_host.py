@@ -179,3 +179,24 @@ def test_min_age_protects_fresh_fills():
         dev.log_misses([2])
         t.step()
     assert fetched == [1, 2] and t.res[1] == 0
+
+
+def test_drop_choice_matches_a_full_sort():
+    """The budget's drop choice (selected in linear time) equals taking the first keys of a full sort by (not in VRAM,
+    resident since, key), over random states with many ties."""
+    rng = np.random.default_rng(5)
+    for trial in range(200):
+        n = int(rng.integers(8, 300))
+        dev = FakeDevice(n_keys=n, cap=8)
+        t, _, _ = _tier(dev, budget=n, min_age=int(rng.integers(0, 4)))
+        t.tick = 20
+        t.state[:] = rng.choice([0, 1, 2], size=n, p=[0.3, 0.1, 0.6])
+        t.since[:] = rng.integers(0, 20, size=n)
+        t.pinned[:] = rng.random(n) < 0.1
+        in_vram = rng.random(n) < 0.3
+        droppable = (t.state == 2) & ~t.pinned & (in_vram | (t.since <= t.tick - t.min_age))
+        want = sorted(np.flatnonzero(droppable).tolist(), key=lambda k: (not in_vram[k], t.since[k], k))
+        n_want = int(rng.integers(0, n))
+        excess = int(np.count_nonzero(t.state != 0)) + n_want - t.budget
+        drop = t._make_room(n_want, in_vram)
+        assert drop.tolist() == want[:max(0, excess)], trial
