@@ -154,7 +154,9 @@ class StoreReader:
 
     def read(self, key: int, out: torch.Tensor) -> None:
         """Record `key`'s blob into `out` (uint8 CPU tensor of >= blob bytes, e.g. a pinned host slot).  With O_DIRECT
-        the read lands in `out` itself when it is page-aligned and holds a whole record, else in a bounce buffer."""
+        the read lands in `out` itself when it is page-aligned and holds a whole record (>= rec bytes): then its
+        bytes from blob to rec receive the record's zero padding, so pass a slot of its own, not a view that runs into
+        the next one.  Otherwise the read goes through a bounce buffer and only the blob's bytes are written."""
         meta = self.meta
         if not 0 <= key < meta.L * meta.E:
             raise IndexError(f"exl3b200 pack_store: key {key} outside {meta.L} x {meta.E}")
