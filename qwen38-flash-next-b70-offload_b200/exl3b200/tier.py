@@ -17,8 +17,12 @@ by the device.  step(), once per decode step after the step's kernels are queued
 
   1. absorbs what happened since: keys the device flagged (victim write-backs) and keys whose fetch reported
      fill_done become resident at this step;
-  2. releases dropped keys once a snapshot taken after a whole decode step past their flag clear has been read (it
-     shows any write-back of the key in that step, which makes it resident again instead);
+  2. releases dropped keys once a snapshot taken after a whole decode step past their flag clear has been read and
+     shows the key out of VRAM.  A key whose expert sits in VRAM is written back to its row (flag set) when its slot
+     is evicted, at any later step; the snapshot that shows the eviction also shows that flag, and the key is resident
+     again instead of released.  Out of VRAM and unflagged, a key cannot come back into VRAM (a fill needs the flag),
+     so nothing writes its row after the release.  RAM use is therefore bounded by budget + VRAM slots: rows of
+     dropped keys still in VRAM are held until they leave it;
   3. reads the keys logged to the miss ring since the previous snapshot (the last cap of them when more were logged);
      the absent ones are wanted, most-logged first, lower key first on ties;
   4. makes room for them, resident + fetching + wanted <= budget, by dropping resident keys that are not pinned:
@@ -119,7 +123,7 @@ class TierHost:
         if snap is not None:
             flags, ring, in_vram = snap
             self._absorb(flags)
-            self._release_dropped()
+            self._release_dropped(in_vram)
             want, logged = self._wanted(ring)
             dropped = self._make_room(len(want), in_vram)
             self._admit(want)
@@ -147,7 +151,7 @@ class TierHost:
         if filled:
             self._become_resident(np.asarray(filled, dtype=np.int64))
 
-    def _release_dropped(self) -> None:
+    def _release_dropped(self, in_vram: np.ndarray) -> None:
         waiting = []
         for when, keys in self._dropped:
             # the snapshot read now was queued at the end of step tick - 1, after decode step tick - 1 >= when + 1
@@ -156,7 +160,12 @@ class TierHost:
                 continue
             back = self.state[keys] != ABSENT
             self.stats["release_rescued"] += int(back.sum())
-            for key in keys[~back].tolist():
+            # a key still in VRAM can be written back whenever its slot is evicted, so its row is released only once
+            # a snapshot shows it out of VRAM: the same snapshot then shows the write-back's flag (rescued above)
+            held = ~back & in_vram[keys]
+            if held.any():
+                waiting.append((when, keys[held]))
+            for key in keys[~back & ~held].tolist():
                 self.release(key)
                 self.stats["released"] += 1
         self._dropped = waiting

@@ -74,7 +74,41 @@ def test_budget_drops_vram_copies_first_then_oldest():
     assert released == []                   # released only after the device ran a step past the clear
     t.step()
     t.step()
+    assert released == [1]                  # 4 is held while its expert sits in VRAM (it may be written back)
+    t.step()
+    assert released == [1]
+    dev.slot_of[4] = -1                     # evicted without a write-back (no victim buffer)
+    t.step()
+    t.step()
     assert sorted(released) == [1, 4]
+
+
+def test_a_dropped_vram_copy_written_back_on_eviction_is_kept():
+    """The race a release must not lose: the RAM copy of a VRAM-resident key is dropped; several steps later its slot
+    is evicted and the victim write-back restores the row and sets the flag.  The row must not be released after
+    that write-back, whenever it lands."""
+    dev = FakeDevice()
+    t, fetched, released = _tier(dev, budget=2)
+    t.step()
+    for key in [3, 5]:
+        dev.log_misses([key])
+        t.step()
+        t.step()
+        t.fill_done(key)
+    t.step()
+    dev.slot_of[3] = 1                      # 3 also sits in VRAM: its RAM copy goes first
+    dev.log_misses([7])
+    t.step()
+    t.step()
+    assert t.res[3] == 0 and fetched[-1] == 7
+    for _ in range(4):                      # held: still in VRAM
+        t.step()
+    assert released == []
+    dev.slot_of[3] = -1                     # evicted during a decode step, written back in the same call
+    dev.victim_writeback(3)
+    t.step()
+    t.step()
+    assert released == [] and t.res[3] == 1 and t.stats["release_rescued"] == 1
 
 
 def test_victim_writeback_becomes_resident_and_rescues_a_drop():

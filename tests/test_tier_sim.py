@@ -1,0 +1,130 @@
+"""CPU: the RAM tier end to end, after the reference harness's "sim" phase (experimental/n111-victim-ring/
+n111_test.py:8, 255-300): small VRAM and RAM tiers, so many evictions, every read checked against the golden data,
+periodic audits of every flagged page.
+
+The device is played by the oracle's cache step (oracle.CacheState.ensure: tier mask, miss ring, LRU slots, victim
+list) over real memory: a slot arena and a RAM-tier arena whose addresses sit in the pointer table.  Fills, victim
+write-backs and reads go through those addresses, as the kernels' copies do.  The host side is the product's own:
+exl3b200.tier.TierHost steps once per decode step, its fetch() is a pack_store.StoreFetcher reading records from a
+store file on reader threads, and its release() zeroes the key's RAM row (the reference punches the page out).
+
+Invariants checked at every call or audit:
+  * every pick, after the mask, reads its own expert's record through the table;
+  * a pick is masked exactly when its expert is in neither VRAM nor RAM;
+  * every key flagged in ram_res has its record in its RAM row, every slot holds its owner's record;
+  * release() is never called for a key whose flag is set.
+"""
+import ctypes
+import mmap
+import time
+
+import numpy as np
+import torch
+
+import oracle as O
+from exl3b200 import pack_store as P
+from exl3b200.tier import TierHost
+
+L, E, S, TOPK, T = 3, 16, 6, 4, 2
+BLOB = 8192 + 320                # not a page multiple: records carry padding
+RING = 16
+
+
+def _record(layer, e):
+    return np.random.default_rng(1000 * layer + e).integers(0, 256, BLOB, dtype=np.uint8)
+
+
+def _aligned(nbytes):
+    return np.frombuffer(mmap.mmap(-1, nbytes), dtype=np.uint8)
+
+
+def _route(rng):
+    """Zipf-skewed picks, distinct per token."""
+    p = 1.0 / np.arange(1, E + 1) ** 1.1
+    perm = rng.permutation(E)
+    return np.stack([perm[rng.choice(E, TOPK, replace=False, p=p / p.sum())] for _ in range(T)]).astype(np.int32)
+
+
+def test_tier_end_to_end(tmp_path):
+    meta = P.StoreMeta.for_blob(L, E, 3, BLOB, 0, 0)
+    P.pack(str(tmp_path), meta, lambda layer, e: _record(layer, e).tobytes())
+    gold = np.stack([_record(k // E, k % E) for k in range(L * E)])
+    rec = meta.rec
+
+    ram = _aligned(L * E * rec).reshape(L * E, rec)              # the RAM tier: one record-sized row per key
+    slots = _aligned(S * BLOB).reshape(S, BLOB)                  # VRAM slots
+    ram_base = ram.ctypes.data
+    host_base = np.array([ram_base + layer * E * rec for layer in range(L)], np.int64)
+    cs = O.CacheState(L, E, S, host_base, slots.ctypes.data, BLOB, hstride=rec)
+
+    ram_res_t = torch.zeros(L * E, dtype=torch.uint8)
+    ring_t = torch.zeros(1 + RING, dtype=torch.int32)
+    rr, rg = ram_res_t.numpy(), ring_t.numpy()
+    safe = np.zeros(L, np.int32)                                 # expert 0 of every layer stays in RAM
+    pinned = np.zeros(L * E, bool)
+    for layer in range(L):
+        key = layer * E
+        ram[key, :BLOB] = gold[key]
+        rr[key] = 1
+        pinned[key] = True
+
+    released, bad_release = [], []
+
+    def release(key):
+        if rr[key]:
+            bad_release.append(key)
+        ram[key] = 0
+        released.append(key)
+
+    def read(addr):
+        return np.frombuffer(ctypes.string_at(int(addr), BLOB), dtype=np.uint8)
+
+    def audit():
+        for key in np.flatnonzero(rr).tolist():
+            assert np.array_equal(ram[key, :BLOB], gold[key]), ("ram row", key)
+        for s in range(S):
+            owner = int(cs.slot_key[s])
+            if owner >= 0:
+                assert np.array_equal(slots[s], gold[owner]), ("slot", s, owner)
+
+    reader = P.StoreReader(str(tmp_path))
+    rng = np.random.default_rng(3)
+    vict = np.zeros(1 + 2 * E, np.int32)
+    n_masked = n_victims = 0
+    with P.StoreFetcher(reader, dest=lambda key: torch.from_numpy(ram[key]), done=lambda key: tier.fill_done(key),
+                        threads=3) as fetcher:
+        tier = TierHost(ram_res_t, ring_t, torch.from_numpy(cs.slot_of), budget=20, fetch=fetcher.fetch,
+                        release=release, pinned=pinned, min_age=2)
+        for step in range(80):
+            for layer in range(L):
+                ids = _route(rng)
+                w = np.full(ids.shape, 1.0 / TOPK, np.float32)
+                keys = layer * E + ids
+                expect_masked = (cs.slot_of[keys] < 0) & (rr[keys] == 0)
+                cs.ensure(ids, w, layer, max_fill=E, ram_res=rr, ring=rg, safe=safe, vict=vict)
+                assert np.array_equal(ids[expect_masked], np.full(expect_masked.sum(), safe[layer]))
+                assert (w[expect_masked] == 0).all() and (w[~expect_masked] > 0).all()
+                n_masked += int(expect_masked.sum())
+                for i in range(int(vict[0])):                  # victim write-back precedes the fills
+                    old, s = int(vict[1 + 2 * i]), int(vict[2 + 2 * i])
+                    if old >= 0:
+                        ram[old, :BLOB] = slots[s]
+                        rr[old] = 1
+                        n_victims += 1
+                for i in range(int(cs.fill_list[0])):          # fills read the host copy the table points at
+                    key = layer * E + int(cs.fill_list[1 + i])
+                    slot = (int(cs.fill_all[key]) - slots.ctypes.data) // BLOB
+                    slots[slot] = read(cs.ptrs_all[key])
+                cs.commit(layer)
+                for e in ids.reshape(-1).tolist():             # every read, through the table
+                    assert np.array_equal(read(cs.ptrs_all[layer * E + e]), gold[layer * E + e]), (step, layer, e)
+            tier.step()
+            if step % 5 == 4:
+                audit()
+            time.sleep(0.002)                                  # lets the reader threads land some fetches
+    reader.close()
+    audit()
+    assert not bad_release
+    st = tier.stats
+    assert n_masked > 0 and st["fetches"] > 0 and st["dropped"] > 0 and len(released) > 0 and n_victims > 0, \
+        (n_masked, dict(st), len(released), n_victims)
