@@ -251,6 +251,18 @@ def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot
     return out
 
 
+def tier_prefetch_ids(ids, layer, n_experts, slot_of, ram_res, safe):
+    """With the RAM tier on, a predicted expert that is in neither VRAM nor RAM has no valid host row to copy from (its
+    row may have been released): it is replaced by the layer's safe expert, which is always resident.  Device ops
+    only, no host sync.  The reference's prefetch mode copies without this test.  Out-of-range ids pass through for the
+    cache step to reject."""
+    if ram_res is None:
+        return ids
+    lookup = ids.long().clamp(0, n_experts - 1) + layer * n_experts
+    ok = (ram_res[lookup] != 0) | (slot_of[lookup] >= 0) | (ids < 0) | (ids >= n_experts)
+    return torch.where(ok, ids, safe[layer].to(ids.dtype)).contiguous()
+
+
 def _moe_prefetch_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base, slot_base, pf_list,
                        pf_slot, max_fill, n_experts, blob):
     """Claim LRU slots for predicted experts (tick not advanced), copy them from host, repoint the table
@@ -261,6 +273,7 @@ def _moe_prefetch_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, tick,
     if S == 0 or ids.numel() == 0:
         return
     mf = min(max_fill, pf_slot.numel())
+    ids = tier_prefetch_ids(ids, layer, E, slot_of, G.ram_res, G.safe)
     ensure(ids, None, layer, E, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob, None,
            pf_list, mf, prefetch=True, pf_slot=pf_slot, tier=False)
     L = _lib.lib()
@@ -301,6 +314,7 @@ def _moe_prefetch_plan_impl(ids, ptrs_all, layer, slot_of, slot_key, slot_last, 
     if pend.numel() < n_layers * _PEND_STRIDE or plan_seq.numel() < n_layers:
         raise RuntimeError("exl3b200 moe_prefetch_plan: pend needs 35 int32 and plan_seq one per layer")
     mf = min(max_fill, _PLAN_MAX, pf_slot.numel())
+    ids = tier_prefetch_ids(ids, layer, E, slot_of, G.ram_res, G.safe)
     check(_lib.lib().exl3b_cepf_plan(ids.data_ptr(), ids.numel(), layer, E, S, ptrs_all.data_ptr(), slot_of.data_ptr(),
                                      slot_key.data_ptr(), slot_last.data_ptr(), tick.data_ptr(), host_base.data_ptr(),
                                      slot_base, blob, G.host_stride or blob, pf_list.data_ptr(), pf_slot.data_ptr(), mf,

@@ -234,3 +234,19 @@ def test_drop_choice_matches_a_full_sort():
         excess = int(np.count_nonzero(t.state != 0)) + n_want - t.budget
         drop = t._make_room(n_want, in_vram)
         assert drop.tolist() == want[:max(0, excess)], trial
+
+
+def test_prefetch_ids_skip_experts_in_neither_tier():
+    """With the RAM tier on, prefetch must not copy an expert whose host row may be released: predictions in neither
+    VRAM nor RAM become the layer's safe expert (exl3b200.ops.tier_prefetch_ids)."""
+    from exl3b200.ops import tier_prefetch_ids
+    E = 8
+    ram_res = torch.zeros(2 * E, dtype=torch.uint8)
+    ram_res[[E + 0, E + 3]] = 1                                    # layer 1: experts 0 (safe) and 3 in RAM
+    slot_of = torch.full((2 * E,), -1, dtype=torch.int32)
+    slot_of[E + 5] = 2                                             # layer 1: expert 5 in VRAM
+    safe = torch.tensor([0, 0], dtype=torch.int32)
+    ids = torch.tensor([3, 5, 6, 1, 9, -1], dtype=torch.int32)     # 9 and -1 are out of range: left to the cache step
+    got = tier_prefetch_ids(ids, 1, E, slot_of, ram_res, safe)
+    assert got.tolist() == [3, 5, 0, 0, 9, -1] and got.dtype == torch.int32
+    assert tier_prefetch_ids(ids, 1, E, slot_of, None, safe) is ids   # tier off: unchanged
