@@ -19,10 +19,12 @@ import mmap
 import time
 
 import numpy as np
+import pytest
 import torch
 
 import oracle as O
 from exl3b200 import pack_store as P
+from exl3b200.ops import tier_prefetch_ids
 from exl3b200.tier import TierHost
 
 L, E, S, TOPK, T = 3, 16, 6, 4, 2
@@ -45,7 +47,11 @@ def _route(rng):
     return np.stack([perm[rng.choice(E, TOPK, replace=False, p=p / p.sum())] for _ in range(T)]).astype(np.int32)
 
 
-def test_tier_end_to_end(tmp_path):
+@pytest.mark.parametrize("prefetch", [False, True])
+def test_tier_end_to_end(tmp_path, prefetch):
+    """prefetch: after each call the next layer's predicted experts are planned for copy-engine prefetch (filtered by
+    tier_prefetch_ids, claimed and pinned by the oracle's plan step); an emulated copy engine lands each plan after a
+    random delay, reading the host rows then, and every call first commits what has landed, as the op does."""
     meta = P.StoreMeta.for_blob(L, E, 3, BLOB, 0, 0)
     P.pack(str(tmp_path), meta, lambda layer, e: _record(layer, e).tobytes())
     gold = np.stack([_record(k // E, k % E) for k in range(L * E)])
@@ -84,13 +90,24 @@ def test_tier_end_to_end(tmp_path):
             assert np.array_equal(ram[key, :BLOB], gold[key]), ("ram row", key)
         for s in range(S):
             owner = int(cs.slot_key[s])
-            if owner >= 0:
+            if owner >= 0 and int(cs.slot_last[s]) != 0x7FFFFFFF:   # a pinned slot's copy may not have landed
                 assert np.array_equal(slots[s], gold[owner]), ("slot", s, owner)
 
     reader = P.StoreReader(str(tmp_path))
     rng = np.random.default_rng(3)
     vict = np.zeros(1 + 2 * E, np.int32)
-    n_masked = n_victims = 0
+    n_masked = n_victims = n_planned = 0
+    cs.cepf_reset()
+    done = np.zeros(L, np.int32)
+    in_flight = []                                             # plans published, not landed: (layer, seq, pairs)
+    safe_t = torch.from_numpy(safe)
+
+    def copy_engine(all_of_them=False):
+        while in_flight and (all_of_them or rng.random() < 0.4):
+            layer, seq, pairs = in_flight.pop(0)
+            for e, s in pairs:
+                slots[s] = ram[layer * E + e, :BLOB]
+            done[layer] = seq
     with P.StoreFetcher(reader, dest=lambda key: torch.from_numpy(ram[key]), done=lambda key: tier.fill_done(key),
                         threads=3) as fetcher:
         tier = TierHost(ram_res_t, ring_t, torch.from_numpy(cs.slot_of), budget=20, fetch=fetcher.fetch,
@@ -100,6 +117,9 @@ def test_tier_end_to_end(tmp_path):
                 ids = _route(rng)
                 w = np.full(ids.shape, 1.0 / TOPK, np.float32)
                 keys = layer * E + ids
+                if prefetch:
+                    copy_engine()
+                    cs.cepf_commit(done)
                 expect_masked = (cs.slot_of[keys] < 0) & (rr[keys] == 0)
                 cs.ensure(ids, w, layer, max_fill=E, ram_res=rr, ring=rg, safe=safe, vict=vict)
                 assert np.array_equal(ids[expect_masked], np.full(expect_masked.sum(), safe[layer]))
@@ -118,11 +138,23 @@ def test_tier_end_to_end(tmp_path):
                 cs.commit(layer)
                 for e in ids.reshape(-1).tolist():             # every read, through the table
                     assert np.array_equal(read(cs.ptrs_all[layer * E + e]), gold[layer * E + e]), (step, layer, e)
+                if prefetch:                                   # predictions for the next layer
+                    nxt = (layer + 1) % L
+                    pred = tier_prefetch_ids(torch.from_numpy(_route(rng).reshape(-1)), nxt, E,
+                                             torch.from_numpy(cs.slot_of), ram_res_t, safe_t).numpy()
+                    r = cs.cepf_plan(pred, nxt, 4, done)
+                    if r is not None and r[1]:
+                        in_flight.append((nxt, r[0], r[1]))
+                        n_planned += len(r[1])
             tier.step()
             if step % 5 == 4:
                 audit()
             time.sleep(0.002)                                  # lets the reader threads land some fetches
     reader.close()
+    if prefetch:
+        copy_engine(all_of_them=True)
+        cs.cepf_commit(done)
+        assert not cs.pend and n_planned > 0
     audit()
     assert not bad_release
     st = tier.stats
