@@ -69,6 +69,13 @@ int exl3b_fill_copy(const int32_t* fill_list, const int64_t* ptrs, const int64_t
 /* Replaces VictimCopyKernel (exl3_moe.a8.sycl:1168-1189): victim slot -> its host address, ram_res[old] = 1. */
 int exl3b_victim_copy(const int32_t* vict, const int64_t* host_base, int64_t slot_base, int64_t blob, int E,
                       int64_t hstride, uint8_t* ram_res, int max_victims, void* stream);
+/* Replaces moe_set_victim_ring (experimental/n111-victim-ring/a9.patch), the victim ring variant of the write-back:
+ * while set (meta != NULL), the victims of exl3b_moe_decode_cached that need a write-back are copied device to device
+ * into free slots of a ring of K blob-sized slots in buf (buf_bytes >= K * blob) instead of to their host rows, and
+ * ram_res is not set; the host drains the ring, flags the keys and frees the slots.  meta: int32 [4 + 2K] on the
+ * device, [next search position, claim sequence, drops (ring full), K, key[K] (-1 free), seq[K]]; sel: int32 on the
+ * device, one entry per victim of a call.  meta = NULL turns the ring off (direct write-back). */
+int exl3b_set_victim_ring(int32_t* meta, int32_t* sel, void* buf, int64_t buf_bytes, int K);
 /* Replaces the cache commit of CombineKernel (exl3_moe.a8.sycl:378-386) and moe_prefetch's table update
  * (:1212-1218): ptrs[e] = fill[e], fill[e] = 0 (or ptrs[e] = slot_base + pf_slot[i]*blob when pf_slot != NULL). */
 int exl3b_commit(const int32_t* fill_list, int64_t* ptrs, int64_t* fill, const int32_t* pf_slot, int64_t slot_base,

@@ -344,3 +344,26 @@ class CacheState:
         if pairs:
             self.pend[layer] = (seq, int(self.tick[0]), pairs)
         return seq, pairs
+
+
+def vring_claim(vict: np.ndarray, meta: np.ndarray, sel: np.ndarray) -> None:
+    """Victim ring claims (the a9 variant of launch_ensure, experimental/n111-victim-ring/a9.patch): in victim-list
+    order, every entry that needs a write-back (old key >= 0) takes the first free slot (key < 0) scanning from the
+    next search position meta[0]; it records key and claim number meta[1] + 1 there and moves the search position
+    past it.  A full ring drops the victim (meta[2] += 1).  sel[i] = the slot of entry i, -1 = no copy.
+    meta = [next position, claim sequence, drops, K, key[K], seq[K]]."""
+    K = int(meta[3])
+    key, seq = meta[4:4 + K], meta[4 + K:4 + 2 * K]
+    p = int(meta[0])
+    for i in range(int(vict[0])):
+        old, r = int(vict[1 + 2 * i]), -1
+        if old >= 0:
+            r = next(((p + j) % K for j in range(K) if key[(p + j) % K] < 0), -1)
+            if r >= 0:
+                meta[1] += 1
+                key[r], seq[r] = old, meta[1]
+                p = (r + 1) % K
+            else:
+                meta[2] += 1
+        sel[i] = r
+    meta[0] = p

@@ -1225,6 +1225,8 @@ static int check_args(const void* x, int64_t x_stride, const int32_t* ids, const
 
 int victim_copy_launch(const int32_t* vict, const int64_t* host_base, int64_t slot_base, int64_t blob, int E,
                        int64_t hstride, uint8_t* ram_res, int max_victims, cudaStream_t s);
+bool vring_active();
+int vring_launch(const int32_t* vict, int64_t slot_base, int64_t blob, int max_victims, cudaStream_t s);
 
 static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int64_t ws_bytes, cudaStream_t s,
                       const int32_t* vict, const int64_t* host_base, int64_t slot_base, int64_t hstride,
@@ -1248,7 +1250,8 @@ static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int6
     cudaError_t e = launch_k(prep_kernel, dim3(1), dim3(1024), 0, s, ea ? *ea : none, a, ea ? 1 : 0);
     if (e != cudaSuccess) return exl3b_fail(EXL3B_ECUDA, cudaGetErrorString(e));
     if (vict && nvict > 0) {   // victim write-back must precede the fill copies that overwrite the slots
-        int rc = victim_copy_launch(vict, host_base, slot_base, a.blob, a.E, hstride, ram_res, nvict, s);
+        int rc = vring_active() ? vring_launch(vict, slot_base, a.blob, nvict, s)
+                                : victim_copy_launch(vict, host_base, slot_base, a.blob, a.E, hstride, ram_res, nvict, s);
         if (rc) return rc;
     }
     // gate-up: clusters of 4 CTAs (2 when H/128 is odd), one per (entry, 128-column block) up to a cap; down: one

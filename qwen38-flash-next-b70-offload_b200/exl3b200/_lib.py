@@ -32,6 +32,7 @@ _SIGS = {
     "exl3b_fill_copy": (ci, [vp, vp, vp, vp, i64, i64, ci, vp]),
     "exl3b_victim_copy": (ci, [vp, vp, i64, i64, ci, i64, vp, ci, vp]),
     "exl3b_commit": (ci, [vp, vp, vp, vp, i64, i64, vp]),
+    "exl3b_set_victim_ring": (ci, [vp, vp, vp, i64, ci]),
     "exl3b_cepf_plan": (ci, [vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, ci, vp, vp, vp, vp, ci,
                              vp]),
     "exl3b_cepf_commit": (ci, [vp, vp, ci, ci, ci, vp, vp, i64, i64, vp]),

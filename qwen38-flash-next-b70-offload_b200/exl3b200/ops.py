@@ -26,6 +26,7 @@ class _Globals:
     ring = None
     safe = None
     vict = None                # moe_set_victims (:767-768): int32 [1 + 2E]
+    vring = None               # moe_set_victim_ring (a9.patch): (meta, sel, buf)
     skip_zero = True           # picks with weight 0 contribute 0: skip them (output unchanged)
 
 
@@ -240,6 +241,8 @@ def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot
     ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
     rr = G.ram_res
     vict = G.vict
+    if vict is not None and G.vring is not None and G.vring[1].numel() < min(max_fill, E):
+        raise RuntimeError("exl3b200 moe_forward_cached: the victim ring's sel needs one entry per possible victim")
     check(L.exl3b_moe_decode_cached(
         x.data_ptr(), x.stride(0), int(x.dtype == torch.bfloat16), topk_ids.data_ptr(), topk_w.data_ptr(), M, topk, layer,
         ptrs_all.data_ptr(), slot_of.data_ptr(), slot_key.data_ptr(), slot_last.data_ptr(), tick.data_ptr(),
@@ -453,6 +456,24 @@ def moe_set_victims(v: torch.Tensor) -> None:
     G.vict = v if v.numel() else None
 
 
+def moe_set_victim_ring(meta: torch.Tensor, sel: torch.Tensor, buf: torch.Tensor) -> None:
+    """moe_set_victim_ring (experimental/n111-victim-ring/a9.patch): victims that need a write-back go device to
+    device into a ring of K = (meta.numel() - 4) / 2 slots of buf instead of to their host rows, and ram_res is not
+    set; the host loop (TierHost with vring) drains the ring and flags the keys.  meta int32 [4 + 2K] (meta[3] = K,
+    keys -1), sel int32 (one entry per victim of a call), buf uint8 [K, blob] on the device.  Empty meta: ring off."""
+    if meta.numel() == 0:
+        check(_lib.lib().exl3b_set_victim_ring(None, None, None, 0, 0), "moe_set_victim_ring")
+        G.vring = None
+        return
+    K = (meta.numel() - 4) // 2
+    if meta.dtype != torch.int32 or sel.dtype != torch.int32 or meta.numel() != 4 + 2 * K or K < 1 or \
+            buf.dtype != torch.uint8 or buf.dim() != 2 or buf.shape[0] != K:
+        raise RuntimeError("exl3b200 moe_set_victim_ring: int32 meta [4 + 2K], int32 sel, uint8 buf [K, blob]")
+    check(_lib.lib().exl3b_set_victim_ring(meta.data_ptr(), sel.data_ptr(), buf.data_ptr(), buf.numel(), K),
+          "moe_set_victim_ring")
+    G.vring = (meta, sel, buf)   # kept referenced while the library holds their addresses
+
+
 def moe_set_tier(ram_res: torch.Tensor, miss: torch.Tensor, safe: torch.Tensor) -> None:
     if ram_res.numel() == 0:
         G.ram_res = G.ring = G.safe = None
@@ -530,6 +551,7 @@ class _Ops:
               "moe_set_debug": moe_set_debug, "moe_set_pair_max_m": moe_set_pair_max_m,
               "moe_set_prefill_min_m": moe_set_prefill_min_m, "moe_set_victims": moe_set_victims,
               "moe_set_tier": moe_set_tier, "moe_set_host_stride": moe_set_host_stride,
+              "moe_set_victim_ring": moe_set_victim_ring,
               "moe_svm_prefetch": moe_svm_prefetch, "moe_prefetch_worker_start": moe_prefetch_worker_start,
               "moe_prefetch_worker_stop": moe_prefetch_worker_stop}.get(name)
         if fn is None:

@@ -214,6 +214,7 @@ class StoreFetcher:
         self.reader, self.dest, self.done = reader, dest, done
         self._q: queue.SimpleQueue = queue.SimpleQueue()
         self._error: BaseException | None = None
+        self._closed = False
         self._threads = [threading.Thread(target=self._run, daemon=True, name=f"exl3b-store-{i}")
                          for i in range(threads)]
         for t in self._threads:
@@ -237,9 +238,14 @@ class StoreFetcher:
 
     def fetch(self, key: int) -> None:
         self._raise()
+        if self._closed:
+            raise RuntimeError("exl3b200 pack_store: fetch after the fetcher was closed")
         self._q.put(int(key))
 
     def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
         for _ in self._threads:
             self._q.put(None)
         for t in self._threads:

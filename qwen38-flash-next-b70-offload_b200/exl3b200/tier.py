@@ -17,12 +17,13 @@ by the device.  step(), once per decode step after the step's kernels are queued
 
   1. absorbs what happened since: keys the device flagged (victim write-backs) and keys whose fetch reported
      fill_done become resident at this step;
-  2. releases dropped keys once a snapshot taken after a whole decode step past their flag clear has been read and
-     shows the key out of VRAM.  A key whose expert sits in VRAM is written back to its row (flag set) when its slot
-     is evicted, at any later step; the snapshot that shows the eviction also shows that flag, and the key is resident
-     again instead of released.  Out of VRAM and unflagged, a key cannot come back into VRAM (a fill needs the flag),
-     so nothing writes its row after the release.  RAM use is therefore bounded by budget + VRAM slots: rows of
-     dropped keys still in VRAM are held until they leave it;
+  2. releases dropped keys once a snapshot taken after a whole decode step past their flag clear has been read.
+     Without a victim ring the snapshot must also show the key out of VRAM: a key whose expert sits in VRAM is written
+     back to its row by the device (flag set) when its slot is evicted, at any later step; the snapshot that shows the
+     eviction also shows that flag, and the key is resident again instead of released.  Out of VRAM and unflagged, a
+     key cannot come back into VRAM (a fill needs the flag), so nothing writes its row after the release; RAM use is
+     bounded by budget + VRAM slots.  With a victim ring (vring) the device never writes rows: evicted victims wait in
+     the ring until this loop drains them, so dropped rows are released at once and RAM use stays within the budget;
   3. reads the keys logged to the miss ring since the previous snapshot (the last cap of them when more were logged);
      the absent ones are wanted, most-logged first, lower key first on ties;
   4. makes room for them, resident + fetching + wanted <= budget, by dropping resident keys that are not pinned:
@@ -45,14 +46,16 @@ import numpy as np
 import torch
 
 ABSENT, FETCHING, RESIDENT = 0, 1, 2
+PINNED_SLOT = 0x7FFFFFFF   # slot_last of a slot claimed by a copy-engine prefetch plan until its copy committed
 
 
 class _Snapshot:
     """One pinned host copy of the device's (ram_res, ring, slot_of), queued behind an event."""
 
-    def __init__(self, ram_res: torch.Tensor, ring: torch.Tensor, slot_of: torch.Tensor, n: int):
+    def __init__(self, ram_res: torch.Tensor, ring: torch.Tensor, slot_of: torch.Tensor, n: int, extras=None):
         self.cuda = ram_res.device.type == "cuda"
-        self.src = (ram_res[:n], ring, slot_of[:n])
+        self.names = list(extras or {})
+        self.src = (ram_res[:n], ring, slot_of[:n]) + tuple((extras or {})[k] for k in self.names)
         self.host = tuple(torch.empty(t.numel(), dtype=t.dtype, pin_memory=self.cuda) for t in self.src)
         self.ready = None       # None before the first queue(); then an event, or True on the CPU
 
@@ -66,18 +69,27 @@ class _Snapshot:
             self.ready = True
 
     def read(self):
-        """(flags, ring, in_vram) as numpy views of the host copy, valid until the next queue(); None before any."""
+        """(flags, ring, slot_of, {name: extra}) as numpy views of the host copy, valid until the next queue(); None
+        before any."""
         if self.ready is None:
             return None
         if self.cuda:
             self.ready.synchronize()
-        flags, ring, slot = (t.numpy() for t in self.host)
-        return flags != 0, ring, slot >= 0
+        flags, ring, slot = (t.numpy() for t in self.host[:3])
+        return flags != 0, ring, slot, {k: t.numpy() for k, t in zip(self.names, self.host[3:])}
 
 
 class TierHost:
     def __init__(self, ram_res: torch.Tensor, ring: torch.Tensor, slot_of: torch.Tensor, budget: int, fetch,
-                 release=None, pinned=None, min_age: int = 0, max_inflight: int | None = None):
+                 release=None, pinned=None, min_age: int = 0, max_inflight: int | None = None, vring=None,
+                 slot_last=None):
+        """vring: (meta, buf, dest) when the decode kernels write victims to a victim ring (ops.moe_set_victim_ring)
+        instead of to host rows: meta / buf are the ring's device tensors, dest(key) the key's host row (uint8, >=
+        blob bytes).  Each step then drains the ring's new claims to their rows on a copy stream; a drained key
+        becomes resident once its copy completed, and its ring slot is freed (key -1 written on the current stream).
+        slot_last: the cache's slot_last tensor.  With a ring, dropped rows are released while their expert sits in
+        VRAM, except a slot pinned by a copy-engine prefetch plan whose copy (which reads the row) has not committed;
+        given slot_last, exactly those are held, else every key still in VRAM is."""
         if ram_res.dtype != torch.uint8 or ring.dtype != torch.int32 or slot_of.dtype != torch.int32:
             raise RuntimeError("exl3b200 TierHost: uint8 ram_res, int32 ring, int32 slot_of")
         if ring.numel() < 2 or slot_of.numel() < ram_res.numel():
@@ -96,7 +108,21 @@ class TierHost:
         self._key_bits = max(1, (self.n - 1).bit_length())  # key field of the packed drop order
         self.tick = 0
         self.ring_seen = int(ring[0].item())
-        self._snap = _Snapshot(ram_res, ring, slot_of, self.n)
+        self._vr = None
+        if vring is not None:
+            meta, buf, dest = vring
+            K = (meta.numel() - 4) // 2
+            if meta.dtype != torch.int32 or meta.numel() != 4 + 2 * K or buf.dim() != 2 or buf.shape[0] != K:
+                raise RuntimeError("exl3b200 TierHost: vring = (int32 meta [4 + 2K], buf [K, blob], dest)")
+            self._vr = {"meta": meta, "buf": buf, "dest": dest, "K": K, "fly": [],
+                        "seen": meta.cpu().numpy()[4 + K:4 + 2 * K].copy(),
+                        "stream": torch.cuda.Stream(meta.device) if meta.is_cuda else None}
+        extras = {}
+        if vring is not None:
+            extras["meta"] = vring[0]
+        if slot_last is not None:
+            extras["slot_last"] = slot_last
+        self._snap = _Snapshot(ram_res, ring, slot_of, self.n, extras=extras)
         self._dropped: list = []                          # [(step of the drop, keys)] awaiting release
         self._done = queue.SimpleQueue()
         self.stats = collections.Counter()
@@ -121,9 +147,12 @@ class TierHost:
         snap = self._snap.read()
         logged = 0
         if snap is not None:
-            flags, ring, in_vram = snap
+            flags, ring, slot, extras = snap
+            in_vram = slot >= 0
             self._absorb(flags)
-            self._release_dropped(in_vram)
+            if self._vr is not None:
+                self._drain_ring(extras["meta"])
+            self._release_dropped(slot, extras.get("slot_last"))
             want, logged = self._wanted(ring)
             dropped = self._make_room(len(want), in_vram)
             self._admit(want)
@@ -151,7 +180,55 @@ class TierHost:
         if filled:
             self._become_resident(np.asarray(filled, dtype=np.int64))
 
-    def _release_dropped(self, in_vram: np.ndarray) -> None:
+    def _drain_ring(self, meta: np.ndarray) -> None:
+        """Victim ring: finished drains make their keys resident and free their slots; new claims are drained."""
+        vr = self._vr
+        K = vr["K"]
+        keys, seqs = meta[4:4 + K], meta[4 + K:4 + 2 * K]
+        free, flying = [], []
+        for ev, r, key in vr["fly"]:
+            if ev is None or ev.query():
+                if self.state[key] != RESIDENT:
+                    self._become_resident([key])
+                self.stats["ring_drained"] += 1
+                free.append(r)
+            else:
+                flying.append((ev, r, key))
+        vr["fly"] = flying
+        for r in np.flatnonzero((keys >= 0) & (seqs != vr["seen"])).tolist():
+            vr["seen"][r] = seqs[r]
+            key = int(keys[r])
+            if not 0 <= key < self.n or self.state[key] == RESIDENT:   # nothing to drain (its row is valid already)
+                free.append(r)
+                continue
+            self.state[key] = FETCHING                                  # not fetched again, not released
+            dst = vr["dest"](key)[: vr["buf"].shape[1]]
+            if vr["stream"] is not None:   # the snapshot just read waited for the decode step that wrote the slot
+                with torch.cuda.stream(vr["stream"]):
+                    dst.copy_(vr["buf"][r], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(vr["stream"])
+            else:
+                dst.copy_(vr["buf"][r])
+                ev = None
+            vr["fly"].append((ev, r, key))
+        if free:
+            idx = torch.tensor([4 + r for r in free], dtype=torch.int64)
+            if vr["meta"].is_cuda:
+                idx = idx.pin_memory().to(vr["meta"].device, non_blocking=True)
+            vr["meta"].index_fill_(0, idx, -1)
+
+    def _held(self, keys: np.ndarray, slot: np.ndarray, slot_last) -> np.ndarray:
+        """Dropped keys whose row must stay (see the module docstring, step 2)."""
+        s = slot[keys]
+        if self._vr is None or slot_last is None:
+            return s >= 0
+        pinned = np.zeros(len(keys), dtype=bool)
+        inside = (s >= 0) & (s < len(slot_last))
+        pinned[inside] = slot_last[s[inside]] == PINNED_SLOT
+        return pinned
+
+    def _release_dropped(self, slot: np.ndarray, slot_last) -> None:
         waiting = []
         for when, keys in self._dropped:
             # the snapshot read now was queued at the end of step tick - 1, after decode step tick - 1 >= when + 1
@@ -160,9 +237,11 @@ class TierHost:
                 continue
             back = self.state[keys] != ABSENT
             self.stats["release_rescued"] += int(back.sum())
-            # a key still in VRAM can be written back whenever its slot is evicted, so its row is released only once
-            # a snapshot shows it out of VRAM: the same snapshot then shows the write-back's flag (rescued above)
-            held = ~back & in_vram[keys]
+            # without a victim ring, a key still in VRAM is written back to its row by the device whenever its slot is
+            # evicted, so its row is released only once a snapshot shows it out of VRAM: the same snapshot then shows
+            # the write-back's flag (rescued above).  With a ring the device never writes rows (the host drains the
+            # ring itself, marking the key fetching first), so the row goes now and the drain brings it back
+            held = ~back & self._held(keys, slot, slot_last)
             if held.any():
                 waiting.append((when, keys[held]))
             for key in keys[~back & ~held].tolist():

@@ -47,11 +47,13 @@ def _route(rng):
     return np.stack([perm[rng.choice(E, TOPK, replace=False, p=p / p.sum())] for _ in range(T)]).astype(np.int32)
 
 
-@pytest.mark.parametrize("prefetch", [False, True])
-def test_tier_end_to_end(tmp_path, prefetch):
+@pytest.mark.parametrize("prefetch,ring", [(False, False), (True, False), (False, True), (True, True)])
+def test_tier_end_to_end(tmp_path, prefetch, ring):
     """prefetch: after each call the next layer's predicted experts are planned for copy-engine prefetch (filtered by
     tier_prefetch_ids, claimed and pinned by the oracle's plan step); an emulated copy engine lands each plan after a
-    random delay, reading the host rows then, and every call first commits what has landed, as the op does."""
+    random delay, reading the host rows then, and every call first commits what has landed, as the op does.
+    ring: victims go to a 3-slot victim ring (oracle.vring_claim) instead of to their rows, unflagged; the host loop
+    drains the ring into the rows and flags them."""
     meta = P.StoreMeta.for_blob(L, E, 3, BLOB, 0, 0)
     P.pack(str(tmp_path), meta, lambda layer, e: _record(layer, e).tobytes())
     gold = np.stack([_record(k // E, k % E) for k in range(L * E)])
@@ -102,6 +104,14 @@ def test_tier_end_to_end(tmp_path, prefetch):
     in_flight = []                                             # plans published, not landed: (layer, seq, pairs)
     safe_t = torch.from_numpy(safe)
 
+    K_RING = 3
+    meta_t = torch.full((4 + 2 * K_RING,), -1, dtype=torch.int32)
+    meta_t[:4] = torch.tensor([0, 0, 0, K_RING], dtype=torch.int32)
+    meta_t[4 + K_RING:] = 0
+    ring_buf = torch.zeros(K_RING, BLOB, dtype=torch.uint8)
+    sel = np.zeros(E, np.int32)
+    vring = (meta_t, ring_buf, lambda key: torch.from_numpy(ram[key])) if ring else None
+
     def copy_engine(all_of_them=False):
         while in_flight and (all_of_them or rng.random() < 0.4):
             layer, seq, pairs = in_flight.pop(0)
@@ -111,7 +121,8 @@ def test_tier_end_to_end(tmp_path, prefetch):
     with P.StoreFetcher(reader, dest=lambda key: torch.from_numpy(ram[key]), done=lambda key: tier.fill_done(key),
                         threads=3) as fetcher:
         tier = TierHost(ram_res_t, ring_t, torch.from_numpy(cs.slot_of), budget=20, fetch=fetcher.fetch,
-                        release=release, pinned=pinned, min_age=2)
+                        release=release, pinned=pinned, min_age=2, vring=vring,
+                        slot_last=torch.from_numpy(cs.slot_last))
         for step in range(80):
             for layer in range(L):
                 ids = _route(rng)
@@ -125,11 +136,16 @@ def test_tier_end_to_end(tmp_path, prefetch):
                 assert np.array_equal(ids[expect_masked], np.full(expect_masked.sum(), safe[layer]))
                 assert (w[expect_masked] == 0).all() and (w[~expect_masked] > 0).all()
                 n_masked += int(expect_masked.sum())
+                if ring:                                       # victims into the ring, unflagged
+                    O.vring_claim(vict, meta_t.numpy(), sel)
                 for i in range(int(vict[0])):                  # victim write-back precedes the fills
                     old, s = int(vict[1 + 2 * i]), int(vict[2 + 2 * i])
-                    if old >= 0:
+                    if old >= 0 and not ring:
                         ram[old, :BLOB] = slots[s]
                         rr[old] = 1
+                        n_victims += 1
+                    elif old >= 0 and sel[i] >= 0:
+                        ring_buf[sel[i]] = torch.from_numpy(slots[s])
                         n_victims += 1
                 for i in range(int(cs.fill_list[0])):          # fills read the host copy the table points at
                     key = layer * E + int(cs.fill_list[1 + i])
@@ -150,6 +166,12 @@ def test_tier_end_to_end(tmp_path, prefetch):
             if step % 5 == 4:
                 audit()
             time.sleep(0.002)                                  # lets the reader threads land some fetches
+        for _ in range(500):                                   # no more decode: every fetch and drain completes
+            tier.step()
+            if not (tier.state == 1).any():
+                break
+            time.sleep(0.005)
+        assert not (tier.state == 1).any(), np.flatnonzero(tier.state == 1)   # nothing left "fetching"
     reader.close()
     if prefetch:
         copy_engine(all_of_them=True)
@@ -160,3 +182,5 @@ def test_tier_end_to_end(tmp_path, prefetch):
     st = tier.stats
     assert n_masked > 0 and st["fetches"] > 0 and st["dropped"] > 0 and len(released) > 0 and n_victims > 0, \
         (n_masked, dict(st), len(released), n_victims)
+    if ring:
+        assert st["ring_drained"] > 0 and int(meta_t[2]) > 0, (dict(st), meta_t.tolist())   # drained, and full at times
