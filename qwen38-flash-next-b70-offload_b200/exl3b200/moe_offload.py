@@ -424,6 +424,9 @@ class ExpertStore:
         `stream` has been waited on: slots for resident experts, the staging buffer for the rest
         (moe_offload.py:305-329)."""
         self._no_copy_prefetch("stage_layer")
+        if _ops.G.ram_res is not None:
+            raise RuntimeError("ExpertStore.stage_layer: the RAM tier is on, so host rows may have been released; "
+                               "stage from the pack store (exl3b200.stage.StoreStager) instead")
         if self._stage[buf] is None:
             self._stage[buf] = torch.empty((self.E, self.blob), dtype=torch.uint8, device=self.dev)
         base = s64(self._stage[buf].data_ptr())

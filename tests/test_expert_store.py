@@ -289,3 +289,15 @@ def test_copy_prefetch_worker_buffers_live_until_stop(monkeypatch):
             with pytest.raises(RuntimeError, match="a copy failed"):
                 ops.moe_prefetch_worker_stop()
         assert ops._worker_keep is None
+
+
+def test_host_row_staging_refused_with_the_ram_tier(fake, monkeypatch):
+    """With the RAM tier on, host rows may have been released: staging from them is refused (StoreStager reads the
+    pack store instead)."""
+    from exl3b200 import ops
+    st, keys = _store()
+    monkeypatch.setattr(ops.G, "ram_res", torch.ones(24, dtype=torch.uint8))
+    with pytest.raises(RuntimeError, match="StoreStager"):
+        st.stage_layer(keys[0], 0, None)
+    with pytest.raises(RuntimeError, match="StoreStager"):
+        st.forward_prefill_staged(keys[0], torch.zeros(1, 64), torch.zeros(1, 1, dtype=torch.int32), torch.ones(1, 1))
