@@ -114,8 +114,9 @@ class TierHost:
             K = (meta.numel() - 4) // 2
             if meta.dtype != torch.int32 or meta.numel() != 4 + 2 * K or buf.dim() != 2 or buf.shape[0] != K:
                 raise RuntimeError("exl3b200 TierHost: vring = (int32 meta [4 + 2K], buf [K, blob], dest)")
+            # claim numbers start at 1: every slot already claimed when the loop starts is drained too
             self._vr = {"meta": meta, "buf": buf, "dest": dest, "K": K, "fly": [],
-                        "seen": meta.cpu().numpy()[4 + K:4 + 2 * K].copy(),
+                        "seen": np.zeros(K, dtype=np.int32),
                         "stream": torch.cuda.Stream(meta.device) if meta.is_cuda else None}
         extras = {}
         if vring is not None:

@@ -250,3 +250,19 @@ def test_prefetch_ids_skip_experts_in_neither_tier():
     got = tier_prefetch_ids(ids, 1, E, slot_of, ram_res, safe)
     assert got.tolist() == [3, 5, 0, 0, 9, -1] and got.dtype == torch.int32
     assert tier_prefetch_ids(ids, 1, E, slot_of, None, safe) is ids   # tier off: unchanged
+
+
+def test_ring_claims_pending_at_start_are_drained():
+    """A victim-ring slot claimed before the host loop started is drained like any other: the row receives the
+    ring slot's bytes, the key becomes resident and the slot is freed."""
+    dev = FakeDevice(n_keys=16)
+    K = 2
+    meta = torch.tensor([1, 1, 0, K, 9, -1, 1, 0], dtype=torch.int32)   # slot 0 claimed by key 9 (claim 1)
+    buf = torch.arange(2 * 64, dtype=torch.uint8).view(2, 64)
+    rows = torch.zeros(16, 64, dtype=torch.uint8)
+    t, _, _ = _tier(dev, vring=(meta, buf, lambda key: rows[key]))
+    t.step()
+    t.step()                                # drained (synchronous on the CPU)
+    assert torch.equal(rows[9], buf[0]) and t.state[9] == 1
+    t.step()                                # the drain has completed: resident, slot freed
+    assert t.res[9] == 1 and dev.ram_res[9] == 1 and meta[4:6].tolist() == [-1, -1]
