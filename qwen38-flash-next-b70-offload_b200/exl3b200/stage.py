@@ -126,3 +126,21 @@ class StoreStager:
         if nq < len(self.order) and self.order[nq] not in self.pending:
             self._kick(self.order[nq])
         return y
+
+
+class TierDriver:
+    """The tier object the plugin drives (the reference's NvTier as called at plugin/sglang_plugin.tier.py:546, 952):
+    step() once per decode step (exl3b200.tier.TierHost.step), stage_forward(store, key, li, x, ids, w) for
+    prefill-size MoE calls (StoreStager.stage_forward)."""
+
+    def __init__(self, host, stager: StoreStager):
+        self.host, self.stager = host, stager
+
+    def step(self) -> int:
+        return self.host.step()
+
+    def stage_forward(self, store, key, li, x, topk_ids, topk_w):
+        if store is not self.stager.store or store.layer_index.get(key) != li:
+            raise RuntimeError(f"exl3b200 TierDriver.stage_forward: {key!r} (layer {li}) is not a layer of the staged "
+                               "store")
+        return self.stager.stage_forward(key, x, topk_ids, topk_w)

@@ -71,3 +71,27 @@ def test_stager_checks_the_store_file(setup, tmp_path):
     with pytest.raises(RuntimeError, match="holds E=9"):
         StoreStager(st, r2)
     r2.close()
+
+
+def test_tier_driver_takes_the_plugin_calls(setup):
+    """The plugin's calls, tier.stage_forward(store, key, li, x, ids, w) and tier.step(), reach the stager and the
+    host loop."""
+    from exl3b200.stage import TierDriver
+    st, keys, row, reader, fake = setup
+
+    class Host:
+        steps = 0
+
+        def step(self):
+            Host.steps += 1
+            return 0
+
+    drv = TierDriver(Host(), StoreStager(st, reader, read_ahead=1, threads=2))
+    ids = torch.tensor([[2, 5]], dtype=torch.int32)
+    key = "model.layers.0.mlp"
+    y = drv.stage_forward(st, key, st.layer_index[key], torch.zeros(1, 64), ids, torch.ones(1, 2))
+    assert np.array_equal(y.numpy(), np.stack([_rec(row[key], 2), _rec(row[key], 5)]))
+    assert drv.step() == 0 and Host.steps == 1
+    with pytest.raises(RuntimeError, match="not a layer"):
+        drv.stage_forward(st, key, st.layer_index[key] + 1, torch.zeros(1, 64), ids, torch.ones(1, 2))
+    drv.stager.close()
