@@ -20,6 +20,7 @@ The store's device tensors may be CPU tensors (tests): copies are then synchrono
 from __future__ import annotations
 
 import concurrent.futures
+import time
 
 import numpy as np
 import torch
@@ -129,15 +130,33 @@ class StoreStager:
 
 
 class TierDriver:
-    """The tier object the plugin drives (the reference's NvTier as called at plugin/sglang_plugin.tier.py:546, 952):
-    step() once per decode step (exl3b200.tier.TierHost.step), stage_forward(store, key, li, x, ids, w) for
-    prefill-size MoE calls (StoreStager.stage_forward)."""
+    """The tier object the plugin drives (the reference's NvTier as called at plugin/sglang_plugin.tier.py:147, 546-550,
+    952-953): step() once per decode step and log_stats (exl3b200.tier.TierHost), stage_forward(store, key, li, x,
+    ids, w) for prefill-size MoE calls (StoreStager), ensure_for_prefill(li, ids) for smaller eager prefill calls, and
+    warm(keys, max_bytes) at start-up."""
 
     def __init__(self, host, stager: StoreStager):
         self.host, self.stager = host, stager
 
     def step(self) -> int:
         return self.host.step()
+
+    def ensure_for_prefill(self, li, topk_ids) -> int:
+        """Eager prefill below the staging threshold: the layer's picked experts made RAM-resident now."""
+        return self.host.ensure_for_prefill(li, topk_ids, self.stager.store.E)
+
+    def warm(self, keys_file, max_bytes):
+        """Fill the RAM tier with keys in the store file's numbering (file layer * E + expert), hottest first, up to
+        max_bytes of rows; returns (experts fetched, seconds)."""
+        st = self.stager.store
+        row_of = {rl: st.layer_index[k] for k, rl in self.stager.record_layer.items()}
+        keys = [row_of[int(k) // st.E] * st.E + int(k) % st.E for k in keys_file if int(k) // st.E in row_of]
+        t0 = time.perf_counter()
+        n = self.host.warm(keys, max_keys=int(max_bytes // st.blob))
+        return n, time.perf_counter() - t0
+
+    def log_stats(self, logger, every: int = 200) -> None:
+        self.host.log_stats(logger, every)
 
     def stage_forward(self, store, key, li, x, topk_ids, topk_w):
         if store is not self.stager.store or store.layer_index.get(key) != li:

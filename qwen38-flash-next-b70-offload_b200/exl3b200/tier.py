@@ -41,6 +41,7 @@ from __future__ import annotations
 
 import collections
 import queue
+import time
 
 import numpy as np
 import torch
@@ -132,6 +133,119 @@ class TierHost:
     def res(self) -> np.ndarray:
         """The host's resident flags (uint8 per key), what it last wrote to ram_res."""
         return (self.state == RESIDENT).astype(np.uint8)
+
+    # ---------------------------------------------------------------- outside the decode loop
+    def _sync_device(self) -> None:
+        if self.ram_res.is_cuda:
+            torch.cuda.synchronize(self.ram_res.device)
+
+    def _upload(self, keys, value: int) -> None:
+        keys = np.asarray(keys, dtype=np.int64)
+        if keys.size:
+            idx = torch.from_numpy(keys)
+            if self.ram_res.is_cuda:
+                idx = idx.pin_memory().to(self.ram_res.device, non_blocking=True)
+            self.ram_res.index_fill_(0, idx, value)
+
+    def _wait_fills(self, keys, timeout: float) -> None:
+        """Block until fill_done arrived for every key of `keys`; other keys' completions met meanwhile count too."""
+        pending = set(int(k) for k in keys)
+        deadline = time.monotonic() + timeout
+        while pending:
+            try:
+                key = self._done.get(timeout=max(0.0, deadline - time.monotonic()))
+            except queue.Empty:
+                raise RuntimeError(f"exl3b200 TierHost: {len(pending)} fills did not complete within {timeout} s")
+            self._become_resident([key])
+            pending.discard(key)
+
+    def _make_room_now(self, n_need: int, keep: np.ndarray) -> None:
+        """Drop resident keys (not pinned, not in `keep`) until n_need more fit in the budget, with the device idle: a
+        fresh snapshot first (victims written back since become resident), flags cleared, rows released at once
+        unless the release rule holds them (then they wait in the release list like any drop)."""
+        excess = int(np.count_nonzero(self.state != ABSENT)) + n_need - self.budget
+        if excess <= 0:
+            return
+        self._sync_device()
+        self._snap.queue()                                  # the device is idle: this snapshot is exact
+        flags, _, slot, extras = self._snap.read()
+        self._absorb(flags)
+        excess = int(np.count_nonzero(self.state != ABSENT)) + n_need - self.budget
+        in_vram = slot >= 0
+        protect = self.pinned.copy()
+        protect[keep] = True
+        saved, self.pinned = self.pinned, protect
+        try:
+            drop = self._make_room(n_need, in_vram)
+        finally:
+            self.pinned = saved
+        if not drop.size:
+            self.stats["prefill_over_budget"] += max(0, excess)
+            return
+        self._upload(drop, 0)
+        self._sync_device()
+        held = self._held(drop, slot, extras.get("slot_last"))
+        for key in drop[~held].tolist():
+            self.release(key)
+            self.stats["released"] += 1
+        if held.any():
+            self._dropped.append((self.tick - 2, drop[held]))   # due now; released once out of VRAM
+        self.stats["prefill_dropped"] += drop.size
+
+    def ensure_for_prefill(self, layer: int, ids, n_experts: int, timeout: float = 120.0) -> int:
+        """Eager prefill below the staging threshold (the reference's NvTier.ensure_for_prefill, nvtier.py:389-457):
+        make every expert that `ids` picks in `layer` RAM-resident now (fetched and waited for), within the budget,
+        and flag it on the device, so the prefill kernels read it from host memory.  When room is needed the device
+        is synchronised first.  Not for use inside CUDA graph capture.  Returns the number of experts fetched."""
+        ids_np = ids.reshape(-1).to("cpu", torch.int64).numpy() if isinstance(ids, torch.Tensor) else np.asarray(ids)
+        ids_np = ids_np[(ids_np >= 0) & (ids_np < n_experts)]
+        keys = np.unique(ids_np) + layer * n_experts
+        need = keys[self.state[keys] == ABSENT]
+        wait = keys[self.state[keys] == FETCHING]
+        self._make_room_now(need.size, keys)
+        for key in need.tolist():
+            self.state[key] = FETCHING
+            self.stats["prefill_fetches"] += 1
+            self.fetch(key)
+        self._wait_fills(np.concatenate([need, wait]), timeout)
+        self._upload(keys, 1)
+        self._snap.queue()        # the next step() must read a snapshot taken after these flag writes
+        return int(need.size)
+
+    def warm(self, keys, max_keys: int | None = None, timeout: float = 600.0) -> int:
+        """Fill the RAM tier with `keys` (hottest first) while the budget (or max_keys) has room, and wait for the
+        fills (the reference's NvTier.warm, nvtier.py:492-509).  Returns the number fetched."""
+        room = self.budget - int(np.count_nonzero(self.state != ABSENT))
+        if max_keys is not None:
+            room = min(room, int(max_keys))
+        todo = []
+        for key in dict.fromkeys(int(k) for k in keys):
+            if len(todo) >= room:
+                break
+            if 0 <= key < self.n and self.state[key] == ABSENT:
+                todo.append(key)
+        for key in todo:
+            self.state[key] = FETCHING
+            self.fetch(key)
+        self._wait_fills(todo, timeout)
+        self._upload(todo, 1)
+        self._snap.queue()        # the next step() must read a snapshot taken after these flag writes
+        return len(todo)
+
+    def log_stats(self, logger, every: int = 200) -> None:
+        """Every `every` steps, log the counters' change since the last report (the reference's NvTier.log_stats)."""
+        steps = self.stats["steps"]
+        if not steps or steps % every:
+            return
+        last = getattr(self, "_logged", collections.Counter())
+        d = {k: v - last.get(k, 0) for k, v in self.stats.items()}
+        n = max(1, d.get("steps", 0))
+        logger.info("exl3b200 tier: last %d steps: masked/step %.2f fetches/step %.2f dropped/step %.2f released %d "
+                    "rescued %d victims kept %d ring drained %d, resident %d of budget %d", n, d.get("masked", 0) / n,
+                    d.get("fetches", 0) / n, d.get("dropped", 0) / n, d.get("released", 0),
+                    d.get("release_rescued", 0), d.get("victims_kept", 0), d.get("ring_drained", 0), self.resident(),
+                    self.budget)
+        self._logged = collections.Counter(self.stats)
 
     def resident(self) -> int:
         return int(np.count_nonzero(self.state == RESIDENT))

@@ -81,10 +81,22 @@ def test_tier_driver_takes_the_plugin_calls(setup):
 
     class Host:
         steps = 0
+        calls = []
 
         def step(self):
             Host.steps += 1
             return 0
+
+        def ensure_for_prefill(self, li, ids, n_experts):
+            Host.calls.append(("ensure", li, n_experts))
+            return 0
+
+        def warm(self, keys, max_keys=None):
+            Host.calls.append(("warm", keys, max_keys))
+            return len(keys)
+
+        def log_stats(self, logger, every=200):
+            Host.calls.append(("log", every))
 
     drv = TierDriver(Host(), StoreStager(st, reader, read_ahead=1, threads=2))
     ids = torch.tensor([[2, 5]], dtype=torch.int32)
@@ -92,6 +104,10 @@ def test_tier_driver_takes_the_plugin_calls(setup):
     y = drv.stage_forward(st, key, st.layer_index[key], torch.zeros(1, 64), ids, torch.ones(1, 2))
     assert np.array_equal(y.numpy(), np.stack([_rec(row[key], 2), _rec(row[key], 5)]))
     assert drv.step() == 0 and Host.steps == 1
+    drv.ensure_for_prefill(1, ids)
+    n, secs = drv.warm([2 * E + 3, 1 * E + 0, 9 * E], 3 * BLOB)     # file layer = store row by default; 9 is none
+    drv.log_stats(None, 50)
+    assert Host.calls == [("ensure", 1, E), ("warm", [2 * E + 3, 1 * E + 0], 3), ("log", 50)] and n == 2
     with pytest.raises(RuntimeError, match="not a layer"):
         drv.stage_forward(st, key, st.layer_index[key] + 1, torch.zeros(1, 64), ids, torch.ones(1, 2))
     drv.stager.close()

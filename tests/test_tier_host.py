@@ -266,3 +266,44 @@ def test_ring_claims_pending_at_start_are_drained():
     assert torch.equal(rows[9], buf[0]) and t.state[9] == 1
     t.step()                                # the drain has completed: resident, slot freed
     assert t.res[9] == 1 and dev.ram_res[9] == 1 and meta[4:6].tolist() == [-1, -1]
+
+
+class _Logger:
+    def __init__(self):
+        self.lines = []
+
+    def info(self, fmt, *args):
+        self.lines.append(fmt % args)
+
+
+def test_ensure_for_prefill_fills_within_budget_and_keeps_protocol():
+    """Eager prefill: the picked experts of the layer become resident and flagged now; room is made from other
+    layers' keys (a VRAM copy first), never this layer's; the next steps neither resurrect the dropped keys nor
+    release a row that is still needed."""
+    E = 4
+    dev = FakeDevice(n_keys=3 * E)
+    fetched = []
+    t = TierHost(dev.ram_res, dev.ring, dev.slot_of, budget=4, fetch=lambda k: (fetched.append(k), t.fill_done(k)),
+                 release=(released := []).append)
+    t.step()
+    assert t.warm([5]) == 1                                              # 5 (layer 1) is the oldest resident key
+    t.step()
+    assert t.warm([0, 1, 5, 9, 10]) == 3 and fetched == [5, 0, 1, 9]     # the budget bounds the warm fill
+    assert dev.ram_res.tolist()[:10] == [1, 1, 0, 0, 0, 1, 0, 0, 0, 1]
+    dev.slot_of[9] = 3                                                   # 9 also sits in VRAM
+    n = t.ensure_for_prefill(1, torch.tensor([[0, 1], [2, 0]]), E)    # layer 1's experts 0-2: keys 4-6
+    assert n == 2 and fetched[-2:] == [4, 6]
+    assert dev.ram_res[[4, 5, 6]].tolist() == [1, 1, 1]                 # this layer's picks: resident, flagged
+    assert t.res[9] == 0 and dev.ram_res[9] == 0                          # the VRAM copy went first ...
+    assert sorted(np.flatnonzero(t.res).tolist()) == [1, 4, 5, 6]        # ... then the oldest of other layers (0)
+    assert released == [0]                                                # 9 is held while in VRAM
+    for _ in range(3):
+        t.step()
+    assert t.res[0] == 0 and t.res[9] == 0 and t.stats["victims_kept"] == 0   # not resurrected
+    dev.slot_of[9] = -1
+    t.step()
+    t.step()
+    assert sorted(released) == [0, 9]
+    log = _Logger()
+    t.log_stats(log, every=1)
+    assert log.lines and "resident 4 of budget 4" in log.lines[0]
