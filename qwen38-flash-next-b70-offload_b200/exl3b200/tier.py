@@ -148,16 +148,19 @@ class TierHost:
             self.ram_res.index_fill_(0, idx, value)
 
     def _wait_fills(self, keys, timeout: float) -> None:
-        """Block until fill_done arrived for every key of `keys`; other keys' completions met meanwhile count too."""
-        pending = set(int(k) for k in keys)
+        """Block until every key of `keys` is resident, taking fill completions as they arrive (a completion may also
+        have been taken already, by a snapshot's absorb: the key's state is what counts)."""
+        keys = np.asarray(keys, dtype=np.int64)
         deadline = time.monotonic() + timeout
-        while pending:
+        while True:
+            pending = int(np.count_nonzero(self.state[keys] != RESIDENT))
+            if not pending:
+                return
             try:
                 key = self._done.get(timeout=max(0.0, deadline - time.monotonic()))
             except queue.Empty:
-                raise RuntimeError(f"exl3b200 TierHost: {len(pending)} fills did not complete within {timeout} s")
+                raise RuntimeError(f"exl3b200 TierHost: {pending} fills did not complete within {timeout} s")
             self._become_resident([key])
-            pending.discard(key)
 
     def _make_room_now(self, n_need: int, keep: np.ndarray) -> None:
         """Drop resident keys (not pinned, not in `keep`) until n_need more fit in the budget, with the device idle: a
@@ -200,6 +203,7 @@ class TierHost:
         ids_np = ids.reshape(-1).to("cpu", torch.int64).numpy() if isinstance(ids, torch.Tensor) else np.asarray(ids)
         ids_np = ids_np[(ids_np >= 0) & (ids_np < n_experts)]
         keys = np.unique(ids_np) + layer * n_experts
+        self._finish_drains()             # keys being drained from the victim ring complete here, not via fill_done
         need = keys[self.state[keys] == ABSENT]
         wait = keys[self.state[keys] == FETCHING]
         self._make_room_now(need.size, keys)
@@ -310,6 +314,8 @@ class TierHost:
             else:
                 flying.append((ev, r, key))
         vr["fly"] = flying
+        self._free_ring_slots(free)
+        free = []
         for r in np.flatnonzero((keys >= 0) & (seqs != vr["seen"])).tolist():
             vr["seen"][r] = seqs[r]
             key = int(keys[r])
@@ -327,11 +333,29 @@ class TierHost:
                 dst.copy_(vr["buf"][r])
                 ev = None
             vr["fly"].append((ev, r, key))
-        if free:
-            idx = torch.tensor([4 + r for r in free], dtype=torch.int64)
-            if vr["meta"].is_cuda:
-                idx = idx.pin_memory().to(vr["meta"].device, non_blocking=True)
-            vr["meta"].index_fill_(0, idx, -1)
+        self._free_ring_slots(free)
+
+    def _free_ring_slots(self, slots) -> None:
+        if slots:
+            meta = self._vr["meta"]
+            idx = torch.tensor([4 + r for r in slots], dtype=torch.int64)
+            if meta.is_cuda:
+                idx = idx.pin_memory().to(meta.device, non_blocking=True)
+            meta.index_fill_(0, idx, -1)
+
+    def _finish_drains(self) -> None:
+        """Wait for every ring drain in flight; their keys become resident and their slots free."""
+        vr = self._vr
+        if vr is None or not vr["fly"]:
+            return
+        if vr["stream"] is not None:
+            vr["stream"].synchronize()
+        for _, _, key in vr["fly"]:
+            if self.state[key] != RESIDENT:
+                self._become_resident([key])
+            self.stats["ring_drained"] += 1
+        self._free_ring_slots([r for _, r, _ in vr["fly"]])
+        vr["fly"] = []
 
     def _held(self, keys: np.ndarray, slot: np.ndarray, slot_last) -> np.ndarray:
         """Dropped keys whose row must stay (see the module docstring, step 2)."""

@@ -163,6 +163,14 @@ def test_tier_end_to_end(tmp_path, prefetch, ring):
                         in_flight.append((nxt, r[0], r[1]))
                         n_planned += len(r[1])
             tier.step()
+            if step % 10 == 7:                                 # an eager prefill call below the staging threshold
+                layer = int(rng.integers(L))
+                picks = rng.integers(0, E, 24).astype(np.int32)
+                tier.ensure_for_prefill(layer, torch.from_numpy(picks), E, timeout=10)
+                for e in np.unique(picks).tolist():             # the prefill kernels read through the table
+                    k = layer * E + e
+                    assert rr[k] == 1 or cs.slot_of[k] >= 0, ("not resident for prefill", k)
+                    assert np.array_equal(read(cs.ptrs_all[k]), gold[k]), ("prefill read", step, k)
             if step % 5 == 4:
                 audit()
             time.sleep(0.002)                                  # lets the reader threads land some fetches
