@@ -121,8 +121,11 @@ def test_tier_end_to_end(tmp_path, prefetch, ring):
     with P.StoreFetcher(reader, dest=lambda key: torch.from_numpy(ram[key]), done=lambda key: tier.fill_done(key),
                         threads=3) as fetcher:
         tier = TierHost(ram_res_t, ring_t, torch.from_numpy(cs.slot_of), budget=20, fetch=fetcher.fetch,
-                        release=release, pinned=pinned, min_age=2, vring=vring,
+                        release=release, pinned=pinned, min_age=2, max_inflight=6, vring=vring,
                         slot_last=torch.from_numpy(cs.slot_last))
+        hot = [layer * E + e for e in (1, 2) for layer in range(L)]
+        assert tier.warm(hot, timeout=10) == len(hot)             # start-up fill of the hottest experts
+        assert all(rr[k] == 1 and np.array_equal(ram[k, :BLOB], gold[k]) for k in hot)
         for step in range(80):
             for layer in range(L):
                 ids = _route(rng)
