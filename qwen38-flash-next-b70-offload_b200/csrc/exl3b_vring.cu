@@ -28,14 +28,19 @@ static VringCfg g_vring;   // process-wide, read at launch (set between calls, l
 
 bool vring_active() { return g_vring.meta != nullptr; }
 
-// Claims in victim-list order, each scanning from the next search position for a free slot (one thread: the victims
-// of a call and K are small).  A slot becomes free only when the host writes key = -1 after draining it.
-__global__ void vring_claim_kernel(const int32_t* __restrict__ vict, int32_t* meta, int32_t* sel, int K) {
-    if (threadIdx.x != 0) return;
+// Claims in victim-list order, each scanning from the next search position for a free slot (serial: the victims of a
+// call and K are small).  A slot becomes free only when the host writes key = -1 after draining it.  Compiled for
+// the device (one thread of vring_claim_kernel) and for the host (exl3b_vring_claim_host, which tests call).
+__host__ __device__ inline void vring_claim(const int32_t* vict, int32_t* meta, int32_t* sel, int K) {
     int32_t* key = meta + 4;
     int32_t* seq = meta + 4 + K;
     int p = meta[0];
-    if (p < 0 || p >= K) { set_error(kErrBounds); p = 0; }
+    if (p < 0 || p >= K) {
+#ifdef __CUDA_ARCH__
+        set_error(kErrBounds);
+#endif
+        p = 0;
+    }
     const int n = vict[0];
     for (int i = 0; i < n; ++i) {
         const int old = vict[1 + 2 * i];
@@ -56,6 +61,10 @@ __global__ void vring_claim_kernel(const int32_t* __restrict__ vict, int32_t* me
         sel[i] = r;
     }
     meta[0] = p;
+}
+
+__global__ void vring_claim_kernel(const int32_t* __restrict__ vict, int32_t* meta, int32_t* sel, int K) {
+    if (threadIdx.x == 0) vring_claim(vict, meta, sel, K);
 }
 
 // Victim slot -> its ring slot, 16 B per thread per step; block = (victim entry, 64 KiB chunk).
@@ -97,4 +106,9 @@ extern "C" EXL3B_API int exl3b_set_victim_ring(int32_t* meta, int32_t* sel, void
     EXL3B_CHECK((((uintptr_t)buf) & 15) == 0, "exl3b_set_victim_ring: buf must be 16-byte aligned");
     g_vring = VringCfg{meta, sel, (int64_t)(uintptr_t)buf, buf_bytes, K};
     return 0;
+}
+
+// Test hook, not part of the drop-in surface: the device's claim rule run on host memory.
+extern "C" EXL3B_API void exl3b_vring_claim_host(const int32_t* vict, int32_t* meta, int32_t* sel, int K) {
+    vring_claim(vict, meta, sel, K);
 }

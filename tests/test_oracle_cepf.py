@@ -66,3 +66,31 @@ def test_max_fill_caps_a_plan_at_sixteen():
     cs.cepf_reset()
     seq, pairs = cs.cepf_plan(np.arange(40, dtype=np.int32), 0, 64, np.zeros(1, np.int32))
     assert len(pairs) == 16 and [e for e, _ in pairs] == list(range(16))
+
+
+def test_victim_ring_claim_rule_matches_the_device_source():
+    """The ring claim rule of csrc/exl3b_vring.cu (its one source compiled for the host, exl3b_vring_claim_host)
+    against oracle.vring_claim on random victim lists and ring states."""
+    import ctypes
+    from exl3b200 import _lib
+    L = _lib.lib()
+    fn = L.exl3b_vring_claim_host
+    fn.restype = None
+    fn.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int]
+    rng = np.random.default_rng(11)
+    for trial in range(300):
+        K = int(rng.integers(1, 9))
+        n = int(rng.integers(0, 12))
+        vict = np.zeros(1 + 2 * 16, np.int32)
+        vict[0] = n
+        vict[1:1 + 2 * n:2] = np.where(rng.random(n) < 0.3, -1, rng.integers(0, 500, n))
+        vict[2:2 + 2 * n:2] = rng.integers(0, 64, n)
+        meta = np.zeros(4 + 2 * K, np.int32)
+        meta[0], meta[1], meta[2], meta[3] = rng.integers(0, K), rng.integers(0, 100), rng.integers(0, 5), K
+        meta[4:4 + K] = np.where(rng.random(K) < 0.5, -1, rng.integers(0, 500, K))
+        meta[4 + K:] = rng.integers(0, 100, K)
+        m_dev, s_dev = meta.copy(), np.full(16, 7, np.int32)
+        m_ora, s_ora = meta.copy(), np.full(16, 7, np.int32)
+        fn(vict.ctypes.data, m_dev.ctypes.data, s_dev.ctypes.data, K)
+        O.vring_claim(vict, m_ora, s_ora)
+        assert np.array_equal(m_dev, m_ora) and np.array_equal(s_dev, s_ora), trial
