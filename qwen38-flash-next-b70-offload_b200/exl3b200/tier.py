@@ -125,7 +125,7 @@ class TierHost:
         if slot_last is not None:
             extras["slot_last"] = slot_last
         self._snap = _Snapshot(ram_res, ring, slot_of, self.n, extras=extras)
-        self._dropped: list = []                          # [(step of the drop, keys)] awaiting release
+        self._drop_tick = np.full(self.n, -1, dtype=np.int64)   # step of a drop whose row awaits release, else -1
         self._done = queue.SimpleQueue()
         self.stats = collections.Counter()
 
@@ -192,7 +192,7 @@ class TierHost:
             self.release(key)
             self.stats["released"] += 1
         if held.any():
-            self._dropped.append((self.tick - 2, drop[held]))   # due now; released once out of VRAM
+            self._drop_tick[drop[held]] = self.tick - 2        # due now; released once the rule allows
         self.stats["prefill_dropped"] += drop.size
 
     def ensure_for_prefill(self, layer: int, ids, n_experts: int, timeout: float = 120.0) -> int:
@@ -276,8 +276,7 @@ class TierHost:
             dropped = self._make_room(len(want), in_vram)
             self._admit(want)
             self._write_flags(flags)
-            if dropped.size:
-                self._dropped.append((self.tick, dropped))
+            self._drop_tick[dropped] = self.tick
         self._snap.queue()
         self.stats["steps"] += 1
         return logged
@@ -368,25 +367,23 @@ class TierHost:
         return pinned
 
     def _release_dropped(self, slot: np.ndarray, slot_last) -> None:
-        waiting = []
-        for when, keys in self._dropped:
-            # the snapshot read now was queued at the end of step tick - 1, after decode step tick - 1 >= when + 1
-            if self.tick < when + 2:
-                waiting.append((when, keys))
-                continue
-            back = self.state[keys] != ABSENT
-            self.stats["release_rescued"] += int(back.sum())
-            # without a victim ring, a key still in VRAM is written back to its row by the device whenever its slot is
-            # evicted, so its row is released only once a snapshot shows it out of VRAM: the same snapshot then shows
-            # the write-back's flag (rescued above).  With a ring the device never writes rows (the host drains the
-            # ring itself, marking the key fetching first), so the row goes now and the drain brings it back
-            held = ~back & self._held(keys, slot, slot_last)
-            if held.any():
-                waiting.append((when, keys[held]))
-            for key in keys[~back & ~held].tolist():
-                self.release(key)
-                self.stats["released"] += 1
-        self._dropped = waiting
+        # due: the snapshot read now was queued at the end of step tick - 1, after decode step tick - 1 >= drop + 1
+        due = np.flatnonzero((self._drop_tick >= 0) & (self._drop_tick <= self.tick - 2))
+        if not due.size:
+            return
+        back = self.state[due] != ABSENT
+        self.stats["release_rescued"] += int(back.sum())
+        self._drop_tick[due[back]] = -1
+        rest = due[~back]
+        # without a victim ring, a key still in VRAM is written back to its row by the device whenever its slot is
+        # evicted, so its row is released only once a snapshot shows it out of VRAM: the same snapshot then shows the
+        # write-back's flag (rescued above).  With a ring the device never writes rows (the host drains the ring
+        # itself, marking the key fetching first), so the row goes now and the drain brings it back
+        go = rest[~self._held(rest, slot, slot_last)]
+        self._drop_tick[go] = -1
+        for key in go.tolist():
+            self.release(key)
+            self.stats["released"] += 1
 
     def _wanted(self, ring: np.ndarray):
         count = int(ring[0])
