@@ -20,6 +20,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -54,8 +55,8 @@ class Clocks:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.p = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv") if os.path.isdir(
-            os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_{os.getpid()}.csv"
+        fd, self.path = tempfile.mkstemp(prefix="exl3b_clocks_", suffix=".csv")
+        os.close(fd)
 
     def start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -79,10 +80,12 @@ class Clocks:
             self.p.kill()
         self.f.close()
         rows = []
-        for line in open(self.path):
-            c = [v.strip() for v in line.split(",")]
-            if len(c) >= 9:
-                rows.append(c)
+        with open(self.path) as f:
+            for line in f:
+                c = [v.strip() for v in line.split(",")]
+                if len(c) >= 9:
+                    rows.append(c)
+        os.unlink(self.path)
         if not rows:
             return None
         sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())

@@ -57,6 +57,9 @@ extern "C" EXL3B_API int exl3b_moe_decode_noalloc(const void* x, int64_t x_strid
                                                   const int32_t* kinfo, int H, int I, int K, int E, void* out,
                                                   int64_t out_stride, int out_bf16, int flags, void* stream) {
     if (M < 0 || topk < 1) return exl3b_fail(EXL3B_EINVAL, "exl3b_moe_decode_noalloc: bad M / topk");
+    // shape errors are reported as such, not as a scratch overflow (the size query returns 0 for them)
+    if (H < 128 || I < 128 || H % 128 || I % 128)
+        return exl3b_fail(EXL3B_EINVAL, "exl3b_moe_decode_noalloc: H, I must be multiples of 128");
     if (M == 0) return 0;
     const int64_t need = exl3b_moe_decode_workspace(M, topk, H, I);
     if (need <= 0 || need > kNoallocScratchBytes)

@@ -188,6 +188,9 @@ class TierHost:
         self._upload(drop, 0)
         self._sync_device()
         held = self._held(drop, slot, extras.get("slot_last"))
+        # a key dropped by an earlier step() may still await its release there; this drop supersedes it (released
+        # below, or re-queued as held), so step() must not release it a second time
+        self._drop_tick[drop] = -1
         for key in drop[~held].tolist():
             self.release(key)
             self.stats["released"] += 1
@@ -318,7 +321,8 @@ class TierHost:
         for r in np.flatnonzero((keys >= 0) & (seqs != vr["seen"])).tolist():
             vr["seen"][r] = seqs[r]
             key = int(keys[r])
-            if not 0 <= key < self.n or self.state[key] == RESIDENT:   # nothing to drain (its row is valid already)
+            # nothing to drain: the row is valid already, or a fetch (or an earlier drain) is writing the same bytes
+            if not 0 <= key < self.n or self.state[key] != ABSENT:
                 free.append(r)
                 continue
             self.state[key] = FETCHING                                  # not fetched again, not released

@@ -1,8 +1,6 @@
-"""GPU tests of two paths that have not yet run on a B200: the victim ring (ops.moe_set_victim_ring with the decode
-chain, TierHost's drain) and StoreStager (prefill streamed from the pack store).  They are skipped unless
-EXL3B_RUN_PENDING=1; both paths are checked on the CPU (tests/test_tier_sim.py, tests/test_stage.py) meanwhile."""
-import os
-
+"""GPU tests of the victim ring (ops.moe_set_victim_ring in the decode chain, TierHost's drain) and StoreStager
+(prefill streamed from the pack store).  Both paths are also checked on the CPU (tests/test_tier_sim.py,
+tests/test_stage.py)."""
 import numpy as np
 import pytest
 import torch
@@ -14,8 +12,7 @@ from exl3b200.stage import StoreStager
 from exl3b200.tier import TierHost
 from test_gpu_parity import DEV, _assert_state, _oracle_state, _route, _store
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("EXL3B_RUN_PENDING") != "1", reason="not yet run on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(autouse=True)

@@ -307,3 +307,48 @@ def test_ensure_for_prefill_fills_within_budget_and_keeps_protocol():
     log = _Logger()
     t.log_stats(log, every=1)
     assert log.lines and "resident 4 of budget 4" in log.lines[0]
+
+
+def test_a_key_dropped_twice_is_released_once():
+    """A key dropped by step() awaits its release there; an eager prefill fetches it again and a later one drops it
+    (released at once).  The pending release of the first drop is void: every drop releases the row exactly once."""
+    E = 4
+    dev = FakeDevice(n_keys=3 * E)
+    t = TierHost(dev.ram_res, dev.ring, dev.slot_of, budget=1, fetch=lambda k: t.fill_done(k),
+                 release=(released := []).append)
+    t.step()
+    assert t.warm([0]) == 1
+    dev.log_misses([2])
+    t.step()
+    t.step()                                  # 0 dropped (its release pending), 2 fetched
+    t.step()
+    assert t.res.tolist()[:3] == [0, 0, 1] and released == []
+    t.ensure_for_prefill(0, torch.tensor([0]), E)   # 0 fetched again: 2 dropped and released at once
+    t.ensure_for_prefill(1, torch.tensor([0]), E)   # key 4 needs the room: 0 dropped and released at once
+    assert released == [2, 0]
+    for _ in range(4):
+        t.step()
+    assert sorted(released) == [0, 2]
+
+
+def test_ring_claim_of_a_key_being_fetched_is_not_copied():
+    """A victim-ring claim for a key whose store fetch is in flight frees its ring slot without a second copy into
+    the row the fetch is writing."""
+    dev = FakeDevice(n_keys=16)
+    K = 2
+    meta = torch.tensor([0, 0, 0, K, -1, -1, 0, 0], dtype=torch.int32)
+    buf = torch.full((2, 64), 7, dtype=torch.uint8)
+    rows = torch.zeros(16, 64, dtype=torch.uint8)
+    t, fetched, _ = _tier(dev, vring=(meta, buf, lambda key: rows[key]))
+    t.step()
+    dev.log_misses([9])
+    t.step()
+    t.step()
+    assert fetched == [9] and t.state[9] == 1          # fetching, not complete
+    meta[4], meta[4 + K] = 9, 1                       # slot 0 claimed by key 9
+    t.step()
+    t.step()                                          # the snapshot that shows the claim
+    assert torch.count_nonzero(rows[9]) == 0 and meta[4].item() == -1 and t.stats["ring_drained"] == 0
+    t.fill_done(9)
+    t.step()
+    assert t.res[9] == 1
