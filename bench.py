@@ -10,6 +10,12 @@ for `value`; `e2e` repeats the step through the public op API with the 48 layer 
 memory and the outputs copied back inside the timed region.  Synthetic data: seeded hash-generated EXL3 blobs,
 N(0,1) activations.  Decode does not shard: under torchrun each rank runs an independent replica.
 
+Further legs of the same line: decode at batch 2 and 4; a decode leg where cache misses fill
+(`fill`: an 8-layer stack whose experts are all RAM-resident, so a miss is copied from pinned host memory into an LRU
+slot inside the step); one prefill layer at 8,192 tokens (configs[2], with and without the router); the expert-parallel
+prefill stack; the mixed-bitrate layer with the gated shared expert (configs[4]: decode T=1 and 4, prefill
+T=2048); CPU baselines of decode and prefill.
+
 --impl reference times the reference path's CPU restatement (oracle/, plain C) on the host cores on a bounded
 sample of the same workload (the reference itself is SYCL for an Intel GPU and cannot run here).
 """
@@ -36,9 +42,42 @@ PF_T = 8192          # configs[2] prefill chunk
 # the same per-layer work (4-layer stack): dram__bytes_read.sum + dram__bytes_write.sum
 GU_TRAFFIC_BS1 = 11997696
 PF_KEY0 = 1 << 20    # blob keys of the prefill layer (distinct from the decode stack's)
+# DRAM bytes (read + write) of one prefill gate-up GEMM launch (prefill_gemm_kernel<0>) on the configs[2] layer at
+# 8,192 tokens, from one ncu capture of the bench's own prefill run (997,299,968 read + 124,593,664 written)
+PF_GU_TRAFFIC = 1121893632
 # router weight std: x . Wr then has the std of a standard Gumbel variable (pi / sqrt(6) = 1.28), so -1.1 ln(rank) +
 # router noise makes each layer's top-10 a Zipf(1.1)-like Plackett-Luce sample and picks miss the 8,000-slot cache
 WR_STD = 1.2825498 / (2048 ** 0.5)
+
+
+def per_layer_slots(li: int, slots: int, layers: int) -> int:
+    """Slots the decode stack gives layer li: its hottest Zipf ranks, slots / layers each (the first slots % layers
+    layers one more)."""
+    return slots // layers + (1 if li < slots % layers else 0)
+
+
+def decode_config(T: int, world: int) -> dict:
+    """The decode workload as both arms report it (same keys, same values)."""
+    return {"workload": f"configs[1]: 48-layer MoE decode stack, batch {T}", "tokens_per_step": T, "layers": L,
+            "H": H, "I": I, "experts": E, "topk": TOPK, "K": K, "slots": S, "keys": L * E,
+            "parallelism": f"replicas x{world}",
+            "router": "in the step: logits x . Wr^T + per-layer Zipf(1.1) bias, softmax top-10",
+            "tier": "ram_res = 0 except each layer's safe expert: a pick in neither VRAM nor RAM is masked (safe "
+                    "expert, weight 0) and logged, no fill runs in the timed step (the 'fill' leg times fills)"}
+
+
+def cpu_info() -> dict:
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    import torch
+    return {"cpu_model": model, "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
 
 
 def peaks():
@@ -110,7 +149,7 @@ def build_stack(dev, T):
     st = ExpertStore(H, I, K, E, S, device=dev, max_layers=L)
     # layer tables without a host arena: non-resident experts are never RAM-resident here (ram_res = 0), so the
     # tier mask guarantees no kernel dereferences their table entry (exl3_moe.a8.sycl:762-765 contract)
-    per = [S // L + (1 if li < S % L else 0) for li in range(L)]
+    per = [per_layer_slots(li, S, L) for li in range(L)]
     keys, slot = [], 0
     ptrs = torch.zeros(L * E, dtype=torch.int64)
     slot_of = torch.full((L * E,), -1, dtype=torch.int32)
@@ -244,7 +283,34 @@ def measure_decode(st, wr, bias, xs, ring, args, dev, local, clocks=True):
             "h2d": int(xs.numel() * 2), "d2h": int(outs.numel() * 2)}
 
 
-def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T):
+def prefill_cpu_baseline(arena, x, ids, w, T, seconds=20.0):
+    """The CPU restatement (oracle/, C, prefill semantics: pick outputs rounded to fp16) on the host cores: the first
+    tokens of the same layer (same blobs, routing and inputs), experts on parallel threads, as many tokens as fit the
+    time budget (at least 256); tok/s of that sample."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.lib()
+    threads = os.cpu_count() or 1
+    blobs_np = arena.cpu().numpy()
+    blobs = [blobs_np[e] for e in range(E)]
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    idn, wn = ids.cpu().numpy(), w.cpu().numpy()
+    t0 = time.perf_counter()
+    O.moe_layer_fast(xb, idn, wn, blobs, H, I, K, y_half=True, threads=threads, rows=np.arange(64))
+    probe = time.perf_counter() - t0
+    n = int(min(T, max(256, 64 * seconds / max(probe, 1e-3) / 2)))
+    n = 64 * max(1, n // 64)
+    t0 = time.perf_counter()
+    O.moe_layer_fast(xb, idn, wn, blobs, H, I, K, y_half=True, threads=threads, rows=np.arange(n))
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 2), "unit": "tok/s (one layer)", "cores": threads, "kind": "port",
+            "sample": f"first {n} of the {T} tokens of the configs[2] layer (same blobs, routing and inputs), experts on "
+                      f"{threads} threads, {dt:.1f} s wall; a rate, not extrapolated", **cpu_info()}
+
+
+def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T, cpu_leg=False):
     """one MoE layer, 8192-token prefill chunk, all 512 experts resident, router logits ~ N(0,1) plus a
     per-expert N(0,1.5) bias.  The layer (moe_forward on the router's picks: the grouped tcgen05 GEMM path) is timed
     with device events; e2e adds the host -> device copy of x and the device -> host copy of the output per call."""
@@ -308,18 +374,31 @@ def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T):
         for k in range(3):
             ph[k].append(evs[k].elapsed_time(evs[k + 1]))
     ph = [sum(v) / len(v) for v in ph]
+    # the layer with its router, as one call sequence (router then MoE), device time
+    e0.record()
+    for _ in range(iters):
+        ids_r, w_r = torch.ops.exl3b200_moe.router_topk(x, wr, bias, TOPK)
+        out = fwd(x, ids_r, w_r, ptrs, I, K, E)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms_router = e0.elapsed_time(e1) / iters
     cnt = torch.bincount(ids.flatten().long(), minlength=E)
     _, tc, src = peaks()
     flops = 2.0 * T * TOPK * 3 * H * I
     gu_flops = 2.0 * T * TOPK * 2 * H * I
     gu_ach = gu_flops / (ph[1] * 1e-3) / 1e12
+    cpu = prefill_cpu_baseline(arena, x, ids, w, T) if cpu_leg else None
     del arena
     return {"tokens": T, "value": round(T * 1000.0 / ms, 1), "unit": "tok/s (one layer)", "ms_per_layer": round(ms, 4),
+            "with_router": {"value": round(T * 1000.0 / ms_router, 1), "unit": "tok/s (one layer, router included)",
+                            "ms_per_layer": round(ms_router, 4), "router_ms": round(router_ms, 3)},
+            "cpu_baseline": cpu,
             "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "layer_frac_of_peak": round(flops / (ms * 1e-3) / 1e12 / tc, 4),
             "e2e": {"value": round(T * 1000.0 / ms_e2e, 1), "unit": "tok/s (one layer)",
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2)},
             "roofline": {"bound": "tensor", "achieved": round(gu_ach, 1), "peak": tc, "unit": "TFLOP/s",
-                         "frac": round(gu_ach / tc, 4), "traffic": None, "kernel": "prefill_gemm_kernel<0>",
+                         "frac": round(gu_ach / tc, 4), "traffic": PF_GU_TRAFFIC if T == PF_T else None,
+                         "kernel": "prefill_gemm_kernel<0>",
                          "peak_source": src + " bf16 burst", "algorithmic_flops_per_launch": gu_flops,
                          "avg_launch_us": round(ph[1] * 1e3, 1)},
             "phase_us": {"align_transform": round(ph[0] * 1e3, 1), "gateup_gemm": round(ph[1] * 1e3, 1),
@@ -391,6 +470,157 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
     return out
 
 
+def measure_fill(dev, args, layers=8):
+    """Decode with cache fills: an 8-layer stack of configs[1] layers (H=2048, I=768, 512 experts, top-10, K=3,
+    Zipf(1.1) routing), the same slots per layer as the 48-layer stack (1,333 here), every expert RAM-resident (the
+    RAM tier holds all keys), so a pick that misses VRAM is copied from its pinned host copy into the LRU slot inside
+    the step (write-through read of the host copy in the same call).  The step is one CUDA graph of router + cached
+    MoE call per layer; the cache state evolves from replay to replay."""
+    import numpy as np
+    import torch
+    from exl3b200 import ExpertStore, synth
+    from exl3b200 import ops as X
+    Sf = round(S * layers / L)
+    st = ExpertStore(H, I, K, E, Sf, device=dev, max_layers=layers)
+    stage = torch.empty((E, BLOB), dtype=torch.uint8, device=dev)
+    synth.fill_blobs(stage, SEED, list(range(E)), H, I, K)
+    host = stage.cpu()
+    del stage
+    keys = []
+    for li in range(layers):
+        key = f"model.layers.{li}.mlp"
+        st.add_layer(key).copy_(host)   # the layers share one set of expert bytes (timing does not depend on them)
+        keys.append(key)
+    del host
+    for li, key in enumerate(keys):
+        st.make_resident(key, synth.zipf_rank(E, li, SEED)[:per_layer_slots(li, Sf, layers)].tolist())
+    ram_res = torch.ones(layers * E, dtype=torch.uint8, device=dev)
+    ring = torch.zeros(1 + 4096, dtype=torch.int32, device=dev)
+    safe = torch.tensor([int(synth.zipf_rank(E, li, SEED)[0]) for li in range(layers)], dtype=torch.int32, device=dev)
+    X.moe_set_tier(ram_res, ring, safe)
+    wr = torch.stack([synth.router_weight(E, H, WR_STD, SEED + 17 * li) for li in range(layers)]).to(dev)
+    bias = torch.stack([synth.zipf_bias(E, li, SEED) for li in range(layers)]).to(dev)
+    # new tokens every step (16 rotating input sets, copied into the step's input buffer before each replay): with
+    # fixed inputs the routing would repeat and every pick would hit after the first step
+    pool = torch.stack([torch.stack([synth.activations(1, H, 20000 + 97 * j + li) for li in range(layers)])
+                        for j in range(16)]).to(dev)
+    xs = pool[0].clone()
+    outs = torch.empty_like(xs)
+
+    def step():
+        for li, key in enumerate(keys):
+            ids, w = torch.ops.exl3b200_moe.router_topk(xs[li], wr[li], bias[li], TOPK)
+            st.forward_cached(key, xs[li], ids, w, out=outs[li])
+
+    try:
+        for j in range(3):
+            xs.copy_(pool[j])
+            step()
+        torch.cuda.synchronize(dev)
+        # fills per layer call over a few eager steps (the fill list of each call, read after it)
+        nf = []
+        for j in range(4):
+            xs.copy_(pool[3 + j])
+            for li, key in enumerate(keys):
+                ids, w = torch.ops.exl3b200_moe.router_topk(xs[li], wr[li], bias[li], TOPK)
+                st.forward_cached(key, xs[li], ids, w, out=outs[li])
+                nf.append(int(st.fill_list[0].item()))
+        g = torch.cuda.CUDAGraph()
+        s2 = torch.cuda.Stream(dev)
+        s2.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s2):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s2)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g):
+            step()
+        for j in range(args.warmup):
+            xs.copy_(pool[j % 16])
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for j in range(args.steps):
+            xs.copy_(pool[(7 + j) % 16])   # 8 KB device copy per step, inside the timed region
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        del g
+    finally:
+        X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32),
+                       torch.zeros(0, dtype=torch.int32))
+    per_layer = ms / layers
+    return {"value": round(1000.0 / ms, 2), "unit": f"tok/s ({layers}-layer stack, batch 1)", "ms_per_step": round(ms, 4),
+            "us_per_layer": round(per_layer * 1e3, 2), "fills_per_layer_call": round(float(np.mean(nf)), 3),
+            "config": f"{layers} configs[1] layers, {Sf} slots ({Sf // layers} per layer, as in the 48-layer stack), "
+                      "every expert RAM-resident (misses fill from pinned host memory in the step), Zipf(1.1) routing, "
+                      "router in the step, one CUDA graph per step, new tokens every step"}
+
+
+def measure_config5(dev, iters=20):
+    """one MoE layer, 512 routed experts with per-tensor K drawn from {2, 3, 4, 5} plus the always-on
+    shared expert (K = 4) behind a sigmoid gate, hidden 2048, intermediate 768, top-10, N(0,1) activations, seed 7:
+    decode at T = 1 and 4 and prefill at T = 2048.  A call is router + shared gate + MoE (moe_forward_shared, which
+    runs the decode kernels below 256 tokens and the prefill GEMMs from 256).  Each call is timed alone with device
+    events after a 256 MB write that evicts L2, with new tokens every call, so its codes come from HBM as in a stack.
+    Roofline: decode on HBM bytes (the K-scaled blobs of the distinct experts read, shared expert included), prefill
+    on tensor FLOPs (2 T (top-k + 1) 3 H I)."""
+    import math
+    import numpy as np
+    import torch
+    from exl3b200 import synth
+    from exl3b200 import ops as X
+    seed = 7
+    kin = [synth.mixed_k(seed, e) for e in range(E)] + [(4, 4, 4)]
+    sizes = [synth.blob_geometry(H, I, *k)["blob"] for k in kin]
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+    arena = torch.empty(int(sum(sizes)), dtype=torch.uint8, device=dev)
+    for e, (k, o, sz) in enumerate(zip(kin, offs, sizes)):
+        synth.fill_blob(arena[int(o):int(o) + sz], seed, e, H, I, *k)
+    ptrs = (arena.data_ptr() + torch.from_numpy(offs)).to(dev)
+    kinfo = torch.tensor([synth.kinfo_pack(*k) for k in kin], dtype=torch.int32, device=dev)
+    gate = synth.router_weight(1, H, 1.0 / math.sqrt(H), seed + 2).reshape(H).to(dev)
+    wr = synth.router_weight(E, H, 1.0 / math.sqrt(H), seed + 3).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    hbm, tc, src = peaks()
+    mean_bpw = float(sum(sizes[:E])) / E / BLOB * K
+    res = {"config": "configs[4]: one layer, 512 routed experts with per-tensor K in {2,3,4,5} (P = .2/.6/.1/.1) plus "
+                     "the shared expert (K=4, sigmoid gate), H=2048, I=768, top-10, seed 7; router and gate in the call; "
+                     "L2 evicted before every call",
+           "mean_routed_code_bits_per_weight_vs_K3_blob": round(mean_bpw, 3)}
+    for T in (1, 4, 2048):
+        xs = [synth.activations(T, H, seed + 100 + 7 * i).to(dev) for i in range(iters + 3)]
+        times, byts = [], []
+        for i, x in enumerate(xs):
+            flush.fill_(i & 255)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ids, w = X.router_topk(x, wr, None, TOPK)
+            torch.ops.exl3b200_moe.moe_forward_shared(x, ids, w, ptrs, kinfo, gate, I, E)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+                used = set(int(v) for v in ids.flatten().tolist()) | {E}
+                byts.append(sum(sizes[e] for e in used))
+        ms = float(np.mean(times))
+        leg = {"value": round(T * 1000.0 / ms, 1), "unit": "tok/s (one layer)", "ms_per_layer": round(ms, 4)}
+        if T < 256:
+            b = float(np.mean(byts))
+            leg["roofline"] = {"bound": "hbm", "achieved": round(b / (ms * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                               "frac": round(b / (ms * 1e-3) / 1e9 / hbm, 4), "bytes_per_call": int(b),
+                               "peak_source": src}
+        else:
+            fl = 2.0 * T * (TOPK + 1) * 3 * H * I
+            leg["roofline"] = {"bound": "tensor", "achieved": round(fl / (ms * 1e-3) / 1e12, 1), "peak": tc,
+                               "unit": "TFLOP/s", "frac": round(fl / (ms * 1e-3) / 1e12 / tc, 4),
+                               "flops_per_call": fl, "peak_source": src + " bf16 burst"}
+        res[("decode_T" if T < 256 else "prefill_T") + str(T)] = leg
+    del arena, flush
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -420,25 +650,38 @@ def run_ours(args):
         dist.barrier()
     d = measure_decode(st, wr, bias, xs, ring, args, dev, local)
     ms, ms_e2e = d["ms"], d["ms_e2e"]
-    bs4 = None
+    batches = {}
     if T == 1 and not args.no_bs4:
-        xs4 = torch.stack([synth.activations(4, H, 1000 + li) for li in range(L)]).to(dev)
-        d4 = measure_decode(st, wr, bias, xs4, ring, args, dev, local, clocks=False)
-        bs4 = {"value": round(world * 4 * 1000.0 / d4["ms"], 2), "unit": "tok/s", "ms_per_step": round(d4["ms"], 4),
-               "e2e": {"value": round(world * 4 * 1000.0 / d4["ms_e2e"], 2), "unit": "tok/s",
-                       "h2d_bytes_per_step": d4["h2d"], "d2h_bytes_per_step": d4["d2h"]},
-               "distinct_experts_per_layer": round(sum(d4["distinct"]) / L, 2),
-               "phase_us": {"route_prep": round(1e3 * sum(d4["rp_ms"]) / len(d4["rp_ms"]), 2),
-                            "gateup": round(1e3 * sum(d4["gu_ms"]) / len(d4["gu_ms"]), 2),
-                            "down_combine": round(1e3 * sum(d4["dn_ms"]) / len(d4["dn_ms"]), 2)}}
-        del xs4
+        for Tb in (2, 4):
+            xb = torch.stack([synth.activations(Tb, H, 1000 + li) for li in range(L)]).to(dev)
+            db = measure_decode(st, wr, bias, xb, ring, args, dev, local, clocks=False)
+            hbm, _, _ = peaks()
+            sb = sum(db["distinct"]) * BLOB
+            batches[f"bs{Tb}"] = {
+                "value": round(world * Tb * 1000.0 / db["ms"], 2), "unit": "tok/s", "ms_per_step": round(db["ms"], 4),
+                "e2e": {"value": round(world * Tb * 1000.0 / db["ms_e2e"], 2), "unit": "tok/s",
+                        "h2d_bytes_per_step": db["h2d"], "d2h_bytes_per_step": db["d2h"]},
+                "distinct_experts_per_layer": round(sum(db["distinct"]) / L, 2),
+                "layer_hbm": {"bytes_per_step": sb, "frac": round(sb / (db["ms"] * 1e-3) / 1e9 / hbm, 4)},
+                "masked_pick_fraction": round(db["masked"], 4),
+                "phase_us": {"route_prep": round(1e3 * sum(db["rp_ms"]) / len(db["rp_ms"]), 2),
+                             "gateup": round(1e3 * sum(db["gu_ms"]) / len(db["gu_ms"]), 2),
+                             "down_combine": round(1e3 * sum(db["dn_ms"]) / len(db["dn_ms"]), 2)}}
+            del xb
     X.moe_set_tier(torch.zeros(0, dtype=torch.uint8), torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32))
+    del st
+    torch.cuda.empty_cache()
+    fill = cfg5 = None
+    if T == 1 and not args.no_fill:
+        fill = measure_fill(dev, args)
+        torch.cuda.empty_cache()
+    if T == 1 and not args.no_config5:
+        cfg5 = measure_config5(dev)
+        torch.cuda.empty_cache()
     pf = pf_ep = None
     if not args.no_prefill:
-        del st
-        torch.cuda.empty_cache()
         if world == 1:
-            pf = measure_prefill(dev, local, T=args.pf_tokens)
+            pf = measure_prefill(dev, local, T=args.pf_tokens, cpu_leg=rank == 0 and not args.no_cpu)
         pf_ep = measure_prefill_ep(dev, local, world, rank, args.ep_tokens)
     hbm, tc, src = peaks()
     distinct = d["distinct"]
@@ -457,11 +700,10 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u32 codes -> fp16 (fp32 accumulate)",
         "data": "synthetic (seeded hash EXL3 blobs, N(0,1) bf16 activations, Zipf(1.1) router bias)",
-        "config": {"workload": f"configs[1]: 48-layer MoE decode stack, batch {T}", "tokens_per_step": T,
-                   "H": H, "I": I, "experts": E, "topk": TOPK, "K": K, "slots": S, "keys": L * E,
-                   "parallelism": f"replicas x{world}", "l2": "working set per step "
-                   f"{step_bytes / 1e6:.0f} MB of codes > 126 MB L2 (no flush needed)",
-                   "masked_pick_fraction": round(d["masked"], 4), "distinct_experts_per_layer": round(avg_distinct, 2)},
+        "config": decode_config(T, world),
+        "workload_stats": {"l2": f"working set per step {step_bytes / 1e6:.0f} MB of codes > 126 MB L2 (no flush "
+                                 "needed)", "masked_pick_fraction": round(d["masked"], 4),
+                           "distinct_experts_per_layer": round(avg_distinct, 2)},
         "e2e": {"value": round(world * T * 1000.0 / ms_e2e, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": d["h2d"], "d2h_bytes_per_step": d["d2h"]},
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
@@ -476,8 +718,11 @@ def run_ours(args):
         "gpu_launches": args.steps * L * 4,
         "clocks": d["clocks"],
     }
-    if bs4 is not None:
-        line["bs4"] = bs4
+    line.update(batches)
+    if fill is not None:
+        line["fill"] = fill
+    if cfg5 is not None:
+        line["config5"] = cfg5
     if pf is not None:
         line["prefill"] = pf
     if pf_ep is not None:
@@ -492,14 +737,6 @@ def run_ours(args):
 
 
 # ------------------------------------------------------------------------------------------------ CPU oracle
-def _oracle_layer_job(args):
-    import numpy as np
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    x, ids, w, blobs = args
-    return O.moe_layer(x, ids, w, blobs, H, I, K)
-
-
 def cpu_baseline(id_buf, w_buf, T, seconds=20.0):
     """The CPU restatement (oracle/, C) on the host cores: layers of the bench step (the GPU run's routing after the
     cache mask; inputs and blobs regenerated from the same seeds) run in parallel threads (the C code releases the
@@ -526,17 +763,44 @@ def cpu_baseline(id_buf, w_buf, T, seconds=20.0):
     with cf.ThreadPoolExecutor(threads) as ex:
         while time.perf_counter() - t0 < seconds and done < 4 * L:
             batch = [jobs[(done + i) % nlay] for i in range(threads)]
-            list(ex.map(_oracle_layer_job, batch))
+            list(ex.map(_oracle_fast_job, batch))
             done += len(batch)
     dt = time.perf_counter() - t0
     tok_s = T * done / L / dt
     return {"value": round(tok_s, 5), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{done} layer calls of the bench step ({T} token(s), top-{TOPK}), {threads} threads, "
-                      f"{dt:.1f} s wall, extrapolated to 48 layers"}
+            "sample": f"{done} layer calls of the bench step ({T} token(s), top-{TOPK}, the GPU run's masked routing), "
+                      f"{threads} threads, {dt:.1f} s wall, extrapolated to 48 layers", **cpu_info()}
+
+
+def tier_mask(ids, w, li):
+    """The decode stack's tier mask on one layer's routing (in place): the stack holds each layer's hottest
+    per_layer_slots Zipf ranks in VRAM and nothing else in RAM, so a pick of a colder expert becomes (safe expert,
+    weight 0), safe = the layer's rank-0 expert; returns the number masked."""
+    import numpy as np
+    from exl3b200 import synth
+    rank_order = synth.zipf_rank(E, li, SEED).numpy()
+    rank = np.empty(E, np.int64)
+    rank[rank_order] = np.arange(E)
+    m = rank[ids] >= per_layer_slots(li, S, L)
+    ids[m] = int(rank_order[0])
+    w[m] = 0.0
+    return int(m.sum())
+
+
+def _oracle_fast_job(args):
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    x, ids, w, blobs = args
+    ids = np.where(w == 0.0, -1, ids).astype(np.int32)   # weight-0 picks contribute exactly 0: not computed (as on the GPU)
+    return O.moe_layer_fast(x, ids, w, blobs, H, I, K, threads=1)
 
 
 def run_reference(args):
-    """--impl reference: the reference path's CPU restatement on host cores; rank 0 only."""
+    """--impl reference: the reference path's CPU restatement (oracle/, C) on the host cores, rank 0 only.  A step
+    runs one layer per host thread (up to 48), each layer one decode call of the bench's stack: the router
+    restatement on the same seeded inputs, the stack's tier mask, the MoE layer.  ms_per_step is the time of those
+    layers; value is tok/s of the 48-layer step, extrapolated from them (also given as its own field)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -549,35 +813,41 @@ def run_reference(args):
     T = args.batch
     threads = os.cpu_count() or 1
     nlay = max(1, min(L, threads))
-    # same seeded workload: routed picks through the CPU router restatement, blobs of the picked experts
-    jobs = []
+    jobs, masked = [], 0
     for li in range(nlay):
         x = synth.activations(T, H, 1000 + li).view(torch.int16).numpy().view(np.uint16)
         wr = synth.router_weight(E, H, WR_STD, SEED + 17 * li).view(torch.int16).numpy().view(np.uint16)
         ids, w, _ = O.router(x, wr, synth.zipf_bias(E, li, SEED).numpy(), TOPK)
+        ids, w = np.ascontiguousarray(ids, np.int32), np.ascontiguousarray(w, np.float32)
+        masked += tier_mask(ids, w, li)
         blobs = [None] * E
-        for e in set(int(v) for v in ids.ravel()):
+        for e in set(int(v) for v, ww in zip(ids.ravel(), w.ravel()) if ww != 0.0):
             blobs[e] = synth.make_blob(SEED, li * E + e, H, I, K).numpy()
         jobs.append((x, ids, w, blobs))
     import concurrent.futures as cf
     times = []
+    t_run = time.perf_counter()
     with cf.ThreadPoolExecutor(threads) as ex:
         for it in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            list(ex.map(_oracle_layer_job, jobs))
+            list(ex.map(_oracle_fast_job, jobs))
             dt = time.perf_counter() - t0
             if it >= args.warmup:
                 times.append(dt)
-    step_s = sum(times) / len(times) * L / nlay
-    v = T / step_s
+    step_s = sum(times) / len(times)
+    full_s = step_s * L / nlay
+    v = T / full_s
     print(json.dumps({
         "metric": METRIC, "value": round(v, 5), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u32 codes -> fp16 (fp64 accumulate)", "impl": "reference",
-        "data": "synthetic (same seeded workload)",
-        "config": {"workload": f"configs[1]: 48-layer MoE decode stack, batch {T}", "tokens_per_step": T},
+        "data": "synthetic (same seeded workload)", "config": decode_config(T, int(os.environ.get("WORLD_SIZE", "1"))),
+        "step": {"layers_per_step": nlay, "ms_per_48_layer_step_extrapolated": round(full_s * 1e3, 1),
+                 "masked_pick_fraction": round(masked / (nlay * T * TOPK), 4),
+                 "run_s": round(time.perf_counter() - t_run, 1)},
         "cpu_baseline": {"value": round(v, 5), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{nlay} of 48 layers per step ({threads} threads), extrapolated to 48 layers"},
+                         "sample": f"{nlay} of the 48 layers per step ({threads} threads, one layer each), "
+                                   "tok/s extrapolated to 48 layers", **cpu_info()},
         "e2e": {"value": round(v, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -590,7 +860,9 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-bs4", action="store_true")
+    ap.add_argument("--no-bs4", action="store_true", help="skip the batch 2 and 4 decode legs")
+    ap.add_argument("--no-fill", action="store_true", help="skip the decode leg whose misses fill")
+    ap.add_argument("--no-config5", action="store_true", help="skip the configs[4] mixed-bitrate layer")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="configs[3] tokens per batch (8192 or 32768)")
     ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
@@ -606,6 +878,8 @@ def main():
     L, S = args.layers, args.slots
     if args.only == "decode":
         args.no_prefill = True
+    if L != 48 or S != 8000:   # small profiling stacks: the headline legs only
+        args.no_fill = args.no_config5 = True
     if args.impl == "reference":
         run_reference(args)
     else:
