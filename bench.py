@@ -435,7 +435,7 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
     torch.cuda.synchronize(dev)
     if world > 1:
         from exl3b200.ep import EPPrefill
-        ep = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs_local)
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs_local, max_tokens=T)
         run = lambda li: ep.forward(xs[li], *routes[li])
     else:
         run = lambda li: X.moe_prefill(xs[li], routes[li][0], routes[li][1], ptrs_local, I, K, E)
@@ -458,6 +458,24 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+    phases, loads = None, None
+    if world > 1:
+        # one more pass with per-phase device events (outside the timed region), and each rank's expert load: the
+        # picks it received over the stack
+        ep.profile = True
+        acc, picks = {}, 0
+        for li in range(layers):
+            run(li)
+            for kname, v in ep.phase_ms().items():
+                acc[kname] = acc.get(kname, 0.0) + v
+            picks += ep.stats()["recv_picks"]
+        ep.profile = False
+        t = torch.tensor([acc[kname] for kname in sorted(acc)] + [float(picks)], dtype=torch.float64, device=dev)
+        allt = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        names = sorted(acc)
+        phases = {n: round(max(float(a[i]) for a in allt) / layers * 1e3, 1) for i, n in enumerate(names)}
+        loads = [int(a[-1]) for a in allt]
     flops = 2.0 * T_total * TOPK * 3 * H * I * layers
     _, tc, _ = peaks()
     out = {"tokens_per_batch": T_total, "layers": layers, "value": round(T_total * 1000.0 / ms, 1),
@@ -465,6 +483,7 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
            "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world, 1),
            "frac_of_peak_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world / tc, 4),
            "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if world > 1 else "one GPU",
+           "phase_us_per_layer_max_over_ranks": phases, "picks_received_per_rank": loads,
            "config": "configs[3]: 48 layers, logits N(0,1) + bias N(0,1.5), top-10, K=3, experts sharded by id"}
     del arena, xs, routes
     return out

@@ -184,6 +184,22 @@ int exl3b_ep_pack(const void* x, int64_t x_stride, int H, const int32_t* send_sr
 int exl3b_ep_combine(const float* part, const int32_t* pos, int T, int G, int H, void* out, int64_t out_stride,
                      int out_kind, void* stream);
 
+/* The exchange EPPrefill runs: one all-to-all of send records each way with equal splits (every rank passes the same
+ * cap >= its T), so the host never reads the counts.  exl3b_ep_record_bytes: bytes of one record, 2 H + 8 topk rounded
+ * up to 16.  exl3b_ep_dispatch: send [G cap] records, destination d's block rows [d cap, (d + 1) cap): its first
+ * counts[d] rows the local tokens that pick d (ascending t), each record the token's row of x (H 16-bit values), then
+ * its topk ids as d's local expert ids (int32, -1 for picks owned elsewhere), then their weights (fp32, 0 for those);
+ * the block's other rows have ids -1 and weights 0 (and an unwritten row of x), so the destination can run its MoE
+ * layer over all G cap received rows.  counts int64 [2 G + 1] (rows per destination, then scratch), pos [T][G] = the
+ * send row of (t, d) or -1, bits [T] and src [G cap] scratch.  exl3b_ep_combine_h: exl3b_ep_combine over fp16 partial
+ * sums (the destinations return [G cap][H] fp16, summed here in fp32 in ascending rank order). */
+int64_t exl3b_ep_record_bytes(int H, int topk);
+int exl3b_ep_dispatch(const void* x, int64_t x_stride, const int32_t* ids, const float* w, int T, int topk, int E, int G,
+                      int H, int cap, uint32_t* bits, int64_t* counts, int32_t* pos, int32_t* src, void* send,
+                      void* stream);
+int exl3b_ep_combine_h(const void* part, const int32_t* pos, int T, int G, int H, void* out, int64_t out_stride,
+                       int out_kind, void* stream);
+
 /* Replaces moe_prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828 with GateUpDpasKernel :422-545, DownDpasKernel
  * :548-635 and CombineKernel :371-395), the path moe_forward takes for M >= prefill_min_m (:1263-1314): the routed-MoE
  * layer for many tokens as grouped tensor-core GEMMs (tcgen05, fp16 operands, fp32 accumulate in TMEM).  Arguments as

@@ -49,6 +49,9 @@ _SIGS = {
     "exl3b_ep_plan": (ci, [vp, vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
     "exl3b_ep_pack": (ci, [vp, i64, ci, vp, ci, vp, vp]),
     "exl3b_ep_combine": (ci, [vp, vp, ci, ci, ci, vp, i64, ci, vp]),
+    "exl3b_ep_record_bytes": (i64, [ci, ci]),
+    "exl3b_ep_dispatch": (ci, [vp, i64, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp]),
+    "exl3b_ep_combine_h": (ci, [vp, vp, ci, ci, ci, vp, i64, ci, vp]),
     "exl3b_shared_gate": (ci, [vp, i64, vp, ci, ci, vp, vp, ci, ci, vp, vp, vp]),
     "exl3b_moe_decode_noalloc": (ci, [vp, i64, ci, vp, vp, ci, ci, vp, vp, ci, ci, ci, ci, vp, i64, ci, ci, vp]),
     "exl3b_moe_prefill_workspace": (i64, [ci, ci, ci, ci, ci]),

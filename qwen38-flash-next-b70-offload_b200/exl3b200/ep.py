@@ -4,16 +4,18 @@ The reference runs its MoE prefill (kernels/moe-a8/exl3_moe.a8.sycl:792-828) on 
 of a torch.distributed group (NCCL on B200s):
 
 * experts are sharded contiguously: rank d owns ids [d E/G, (d+1) E/G) and holds only their blobs;
-* every rank routes its own tokens; a token is sent once to every rank owning at least one of its picks, with the
-  picks as that rank's local ids (-1 for picks owned elsewhere) and their weights (all-to-all of counts, rows, ids,
-  weights);
-* each rank runs the grouped prefill GEMMs (or the decode kernels for few rows) on what it received, returning fp32
-  partial sums per received row (all-to-all back);
-* the source sums a token's partials over the ranks in ascending rank order (exl3b_ep_combine).
+* every rank routes its own tokens and sends each token once to every rank owning at least one of its picks: one
+  record per (token, destination) holding the token's row of x, its picks as the destination's local expert ids (-1 for
+  picks owned elsewhere) and their weights (exl3b_ep_dispatch);
+* the records go in fixed-capacity blocks of `cap` rows per destination (cap >= every rank's token count, the same on
+  all ranks), unused rows marked "no pick", so one all-to-all with equal splits moves them and no rank has to read the
+  counts on the host: a layer queues without a host synchronisation;
+* each rank runs the grouped prefill GEMMs (or the decode kernels for few rows) over all G cap received rows (unused
+  rows have no picks and cost nothing) and returns fp16 partial sums per row with a second all-to-all;
+* the source sums a token's partials over the ranks in ascending rank order (exl3b_ep_combine_h), in fp32.
 
-Every rank takes the same collective steps in the same order.  The device steps go through the C ABI
-(exl3b_ep_plan / _pack / _combine and the MoE entry points); `kernels` may replace them (the CPU tests use a host
-implementation of the same contract to check the exchange protocol on gloo ranks).
+Every rank takes the same collective steps in the same order.  The device steps go through the C ABI; `kernels` may
+replace them (the CPU tests use a host implementation of the same contract to run the exchange on gloo ranks).
 """
 from __future__ import annotations
 
@@ -60,22 +62,60 @@ class CudaEPKernels:
         return out
 
     def local(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, ptrs: torch.Tensor, kinfo, I: int, K: int,
-              n_local: int) -> torch.Tensor:
+              n_local: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         from . import ops
-        out = torch.empty((x.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
+        out = torch.empty((x.shape[0], x.shape[1]), dtype=dtype, device=x.device)
         if x.shape[0] == 0:
             return out
         if x.shape[0] >= ops.G.prefill_min_m and x.shape[1] % 256 == 0:
             return ops.moe_prefill(x, ids, w, ptrs, I, K, n_local, kinfo=kinfo, out=out)
         return ops.moe_decode(x, ids, w, ptrs, I, K, n_local, kinfo=kinfo, out=out)
 
+    # ---- the exchange EPPrefill runs
+    def dispatch(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, n_experts: int, G: int, cap: int) -> dict:
+        """Send records [G cap, record bytes] (uint8), pos [T, G] and counts [G] (int64, on the device)."""
+        T, topk = ids.shape
+        H = x.shape[1]
+        dev = x.device
+        rec = int(_lib.lib().exl3b_ep_record_bytes(H, topk))
+        send = torch.empty((G * cap, rec), dtype=torch.uint8, device=dev)
+        counts = torch.empty(2 * G + 1, dtype=torch.int64, device=dev)
+        pos = torch.empty((max(T, 1), G), dtype=torch.int32, device=dev)
+        bits = torch.empty(max(T, 1), dtype=torch.int32, device=dev)
+        src = torch.empty(G * cap, dtype=torch.int32, device=dev)
+        check(_lib.lib().exl3b_ep_dispatch(x.data_ptr() if T else None, x.stride(0) if T else H,
+                                           ids.data_ptr() if T else None, w.data_ptr() if T else None, T, topk,
+                                           n_experts, G, H, cap, bits.data_ptr(), counts.data_ptr(), pos.data_ptr(),
+                                           src.data_ptr(), send.data_ptr(), stream(dev)), "ep_dispatch")
+        return {"send": send, "pos": pos, "counts": counts[:G]}
+
+    def combine_h(self, part: torch.Tensor, pos: torch.Tensor, T: int, G: int, H: int, dtype: torch.dtype) -> torch.Tensor:
+        out = torch.empty((T, H), dtype=dtype, device=pos.device)
+        code = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}[dtype]
+        check(_lib.lib().exl3b_ep_combine_h(part.data_ptr() if part.numel() else None, pos.data_ptr(), T, G, H,
+                                            out.data_ptr(), out.stride(0), code, stream(pos.device)), "ep_combine_h")
+        return out
+
+
+def unpack_records(recv: torch.Tensor, H: int, topk: int, dtype: torch.dtype):
+    """Received records -> (x rows as a strided view [rows, H] of `dtype`, contiguous int32 ids and fp32 weights
+    [rows, topk])."""
+    x = recv[:, :2 * H].view(dtype)
+    ids = recv[:, 2 * H:2 * H + 4 * topk].view(torch.int32).contiguous()
+    w = recv[:, 2 * H + 4 * topk:2 * H + 8 * topk].view(torch.float32).contiguous()
+    return x, ids, w
+
 
 class EPPrefill:
     """One MoE layer's expert-parallel prefill on this rank: ptrs_local holds the int64 blob addresses of the rank's
-    n_experts / G experts (kinfo_local their packed K when mixed)."""
+    n_experts / G experts (kinfo_local their packed K when mixed).  max_tokens: the token count no rank exceeds in a
+    call, the same on every rank (the record blocks' capacity); without it each call first agrees on the largest token
+    count with one small all-reduce, which reads the result on the host.  profile=True records CUDA events around the
+    phases of each call (read with phase_ms())."""
 
     def __init__(self, group, n_experts: int, H: int, I: int, K: int, ptrs_local: torch.Tensor,
-                 kinfo_local: torch.Tensor | None = None, kernels=None):
+                 kinfo_local: torch.Tensor | None = None, kernels=None, max_tokens: int | None = None,
+                 profile: bool = False):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -87,37 +127,78 @@ class EPPrefill:
             raise RuntimeError("exl3b200 EPPrefill: ptrs_local must hold this rank's n_experts / G blob addresses")
         self.ptrs_local, self.kinfo_local = ptrs_local, kinfo_local
         self.k = kernels or CudaEPKernels()
+        self.max_tokens = max_tokens
+        self.profile = profile
         self.last = {}
+        self._ev = []
 
-    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits):
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor):
         # A peer that stopped (exited, or stuck past the group's timeout) fails the collective; the error names the
         # layer step so that the caller can tell a lost rank from a bad argument.
         try:
-            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+            dist.all_to_all_single(out, inp, group=self.group)
         except RuntimeError as e:   # torch's distributed backend errors derive from RuntimeError
             raise RuntimeError(f"exl3b200 EPPrefill: all-to-all failed on rank {self.rank} of {self.G} "
                                f"(a peer rank stopped or timed out): {e}") from e
 
+    def _cap(self, T: int, device) -> int:
+        if self.max_tokens is not None:
+            if T > self.max_tokens:
+                raise RuntimeError(f"exl3b200 EPPrefill: {T} tokens > max_tokens {self.max_tokens}")
+            return max(1, int(self.max_tokens))
+        t = torch.tensor([T], dtype=torch.int64, device=device)
+        try:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        except RuntimeError as e:
+            raise RuntimeError(f"exl3b200 EPPrefill: token-count all-reduce failed on rank {self.rank} of {self.G} "
+                               f"(a peer rank stopped or timed out): {e}") from e
+        return max(1, int(t.item()))
+
+    def _mark(self, dev):
+        if self.profile and dev.type == "cuda":
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._ev.append(ev)
+
+    def phase_ms(self) -> dict:
+        """Device time of the last profiled call's phases (synchronises): dispatch, all-to-all out, local MoE,
+        all-to-all back, combine."""
+        if len(self._ev) != 6:
+            return {}
+        self._ev[-1].synchronize()
+        names = ["dispatch", "a2a_out", "local_moe", "a2a_back", "combine"]
+        return {n: self._ev[i].elapsed_time(self._ev[i + 1]) for i, n in enumerate(names)}
+
+    def stats(self) -> dict:
+        """Rows and picks of the last call (reads the device): rows sent to / received from each rank, this rank's
+        received picks (its expert load)."""
+        sc = [int(v) for v in self.last["send_counts"].cpu()]
+        idr, cap = self.last["recv_ids"], self.last["cap"]
+        valid = (idr >= 0).any(dim=1).view(self.G, cap)
+        rc = [int(v) for v in valid.sum(dim=1).cpu()]
+        return {"cap": cap, "send_counts": sc, "recv_counts": rc, "send_rows": sum(sc), "recv_rows": sum(rc),
+                "recv_picks": int((idr >= 0).sum().item())}
+
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         G, H = self.G, self.H
         T, topk = ids.shape
-        p = self.k.plan(ids, w, self.E, G)
-        send_counts = p["counts"]
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, None, None)
-        both = torch.stack([send_counts, recv_counts]).cpu()
-        sc, rc = [int(v) for v in both[0]], [int(v) for v in both[1]]
-        n_send, n_recv = sum(sc), sum(rc)
-        send_x = self.k.pack(x, p["send_src"], n_send)
-        recv_x = torch.empty((n_recv, H), dtype=x.dtype, device=x.device)
-        self._a2a(recv_x, send_x, rc, sc)
-        recv_ids = torch.empty((n_recv, topk), dtype=torch.int32, device=x.device)
-        self._a2a(recv_ids, p["send_ids"][:n_send].contiguous(), rc, sc)
-        recv_w = torch.empty((n_recv, topk), dtype=torch.float32, device=x.device)
-        self._a2a(recv_w, p["send_w"][:n_send].contiguous(), rc, sc)
-        part_recv = self.k.local(recv_x, recv_ids, recv_w, self.ptrs_local, self.kinfo_local, self.I, self.K,
-                                 self.n_local)
-        part_send = torch.empty((n_send, H), dtype=torch.float32, device=x.device)
-        self._a2a(part_send, part_recv, sc, rc)
-        self.last = {"send_rows": n_send, "recv_rows": n_recv, "send_counts": sc, "recv_counts": rc}
-        return self.k.combine(part_send, p["pos"], T, G, H, x.dtype)
+        dev = x.device
+        cap = self._cap(T, dev)
+        self._ev = []
+        self._mark(dev)
+        p = self.k.dispatch(x, ids, w, self.E, G, cap)
+        self._mark(dev)
+        recv = torch.empty_like(p["send"])
+        self._a2a(recv, p["send"])
+        self._mark(dev)
+        xr, idr, wr = unpack_records(recv, H, topk, x.dtype)
+        part = self.k.local(xr, idr, wr, self.ptrs_local, self.kinfo_local, self.I, self.K, self.n_local,
+                            dtype=torch.float16)
+        self._mark(dev)
+        back = torch.empty_like(part)
+        self._a2a(back, part)
+        self._mark(dev)
+        out = self.k.combine_h(back, p["pos"], T, G, H, x.dtype)
+        self._mark(dev)
+        self.last = {"cap": cap, "send_counts": p["counts"], "recv_ids": idr}
+        return out

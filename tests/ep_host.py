@@ -1,6 +1,6 @@
 """Test double of the expert-parallel device steps (exl3b200.ep.CudaEPKernels) on host tensors, with the oracle as the
 local expert compute: lets the CPU tests run the EPPrefill exchange protocol on gloo ranks.  Same contract as
-exl3b_ep_plan / _pack / _combine (include/exl3b200.h)."""
+exl3b_ep_plan / _pack / _combine and exl3b_ep_dispatch / _combine_h (include/exl3b200.h)."""
 from __future__ import annotations
 
 import numpy as np
@@ -45,13 +45,47 @@ class HostEPKernels:
     def pack(self, x, send_src, n_rows):
         return x[send_src[:n_rows].long()].contiguous()
 
-    def local(self, x, ids, w, ptrs, kinfo, I, K, n_local):
+    def local(self, x, ids, w, ptrs, kinfo, I, K, n_local, dtype=torch.float32):
         if x.shape[0] == 0:
-            return torch.zeros((0, self.H), dtype=torch.float32)
+            return torch.zeros((0, self.H), dtype=dtype)
         xb = x.contiguous().view(torch.int16).numpy().view(np.uint16)
         part = O.moe_layer_fast(xb, ids.numpy(), w.numpy(), self.blobs, self.H, self.I, self.K, out_f32=True,
                                 y_half=True, threads=2)
-        return torch.from_numpy(part)
+        return torch.from_numpy(part).to(dtype)
+
+    @staticmethod
+    def record_bytes(H, topk):
+        return (2 * H + 8 * topk + 15) // 16 * 16
+
+    def dispatch(self, x, ids, w, n_experts, G, cap):
+        idn, wn = ids.numpy(), w.numpy()
+        T, topk = idn.shape
+        H = x.shape[1]
+        per = n_experts // G
+        rec = self.record_bytes(H, topk)
+        send = np.zeros((G * cap, rec), dtype=np.uint8)
+        send[:, 2 * H:2 * H + 4 * topk] = np.full((G * cap, topk), -1, np.int32).view(np.uint8)
+        pos = np.full((max(T, 1), G), -1, dtype=np.int32)
+        counts = np.zeros(G, dtype=np.int64)
+        xb = x.contiguous().view(torch.int16).numpy().view(np.uint8).reshape(T, 2 * H) if T else None
+        owner = np.where(idn >= 0, idn // per, -1)
+        for d in range(G):
+            j = 0
+            for t in range(T):
+                mine = owner[t] == d
+                if not mine.any():
+                    continue
+                r = d * cap + j
+                pos[t, d] = r
+                send[r, :2 * H] = xb[t]
+                send[r, 2 * H:2 * H + 4 * topk] = np.where(mine, idn[t] - d * per, -1).astype(np.int32).view(np.uint8)
+                send[r, 2 * H + 4 * topk:2 * H + 8 * topk] = np.where(mine, wn[t], 0.0).astype(np.float32).view(np.uint8)
+                j += 1
+            counts[d] = j
+        return {"send": torch.from_numpy(send), "pos": torch.from_numpy(pos), "counts": torch.from_numpy(counts)}
+
+    def combine_h(self, part, pos, T, G, H, dtype):
+        return self.combine(part.to(torch.float32), pos, T, G, H, dtype)
 
     def combine(self, part, pos, T, G, H, dtype):
         out = torch.zeros((T, H), dtype=torch.float32)

@@ -49,13 +49,14 @@ def _worker(rank, world, port, case, q):
         w = (w / w.sum(1, keepdim=True)).float() if T else torch.zeros((0, topk))
         x = synth.activations(T, H, 200 + rank) if T else torch.zeros((0, H), dtype=torch.bfloat16)
         k = HostEPKernels(blobs[rank * per:(rank + 1) * per], H, I, K)
-        ep = EPPrefill(dist.group.WORLD, E, H, I, K, torch.zeros(per, dtype=torch.int64), kernels=k)
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, torch.zeros(per, dtype=torch.int64), kernels=k,
+                       max_tokens=case.get("max_tokens"))
         out = ep.forward(x, ids, w)
         if T:
             xb = x.view(torch.int16).numpy().view(np.uint16)
             ref = O.moe_layer_fast(xb, ids.numpy(), w.numpy(), blobs, H, I, K, y_half=True, threads=2)
             assert_close_layer(out.view(torch.int16).numpy().view(np.uint16), ref)
-        q.put((rank, "ok", ep.last))
+        q.put((rank, "ok", ep.stats()))
     except Exception as e:   # reported to the parent
         q.put((rank, f"{type(e).__name__}: {e}", None))
     finally:
@@ -80,6 +81,14 @@ def _run(case, world=2):
 def test_ep_exchange_two_ranks():
     last = _run({"T": [7, 5]})
     assert last[0]["send_rows"] > 0 and last[1]["recv_rows"] > 0
+    assert last[0]["cap"] == last[1]["cap"] == 7   # agreed by the ranks: the largest token count
+
+
+def test_ep_exchange_fixed_capacity():
+    """A capacity given to every rank (max_tokens) instead of agreed per call: the same exchange, no host read."""
+    last = _run({"T": [7, 5], "max_tokens": 9})
+    assert last[0]["cap"] == last[1]["cap"] == 9
+    assert [last[d]["recv_counts"][0] for d in range(2)] == last[0]["send_counts"]
 
 
 def test_ep_rank_without_tokens():

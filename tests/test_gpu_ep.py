@@ -1,4 +1,5 @@
-"""GPU: the expert-parallel device steps (exl3b_ep_plan / _pack / _combine with the local grouped prefill).
+"""GPU: the expert-parallel device steps (exl3b_ep_plan / _pack / _combine, and the exchange EPPrefill runs:
+exl3b_ep_dispatch / _combine_h, with the local grouped prefill).
 
 On one GPU a single source serves G virtual ranks: the plan tables equal the host reference bit for bit, and the
 layer output equals the one-device prefill and the oracle within the layer tolerance.  With two or more GPUs the
@@ -75,6 +76,43 @@ def test_ep_device_steps_single_source(G, T):
     if semantics_prefill:
         one = X.moe_prefill(xd, idd, wd, ptrs, I, K, E, out=torch.empty(T, H, dtype=torch.float32, device=DEV))
         assert_close_f32(out.cpu().numpy(), one.cpu().numpy())
+
+
+@pytest.mark.parametrize("G,T,cap", [(2, 300, 300), (4, 520, 600), (8, 64, 64)])
+def test_ep_dispatch_records_and_fp16_combine(G, T, cap):
+    """The exchange EPPrefill runs, on one GPU with one source serving G virtual ranks: the send records (fixed-capacity
+    blocks, unused rows with no picks) equal the host contract byte for byte on every row a receiver reads, each
+    destination's MoE over its whole block returns fp16 partial sums, and their combine equals the one-device prefill
+    and the oracle within the layer tolerance."""
+    from exl3b200.ep import unpack_records
+    H, I, E, topk, K = 256, 256, 16, 4, 3
+    arena, ptrs, views = make_layer(E, H, I, K, seed=50 + G)
+    x = synth.activations(T, H, 51 + G)
+    ids, w = _route(T, E, topk, 52 + G)
+    xd, idd, wd = x.to(DEV), ids.to(DEV), w.to(DEV)
+    k = CudaEPKernels()
+    p = k.dispatch(xd, idd, wd, E, G, cap)
+    ref = HostEPKernels([], H, I, K).dispatch(x, ids, w, E, G, cap)
+    assert np.array_equal(p["pos"].cpu().numpy()[:T], ref["pos"].numpy()[:T])
+    assert np.array_equal(p["counts"].cpu().numpy(), ref["counts"].numpy())
+    sd, sr = p["send"].cpu().numpy(), ref["send"].numpy()
+    assert sd.shape == sr.shape
+    assert np.array_equal(sd[:, 2 * H:], sr[:, 2 * H:])                     # ids and weights of every row
+    counts = ref["counts"].numpy()
+    for d in range(G):                                                     # rows of x where they are used
+        r0 = d * cap
+        assert np.array_equal(sd[r0:r0 + counts[d], :2 * H], sr[r0:r0 + counts[d], :2 * H])
+    per = E // G
+    blocks = []
+    for d in range(G):
+        xr, idr, wr = unpack_records(p["send"][d * cap:(d + 1) * cap], H, topk, xd.dtype)
+        blocks.append(k.local(xr, idr, wr, ptrs[d * per:(d + 1) * per].contiguous(), None, I, K, per,
+                              dtype=torch.float16))
+    out = k.combine_h(torch.cat(blocks), p["pos"], T, G, H, torch.float32)
+    torch.cuda.synchronize()
+    blobs = [views[e].cpu().numpy() for e in range(E)]
+    ref32 = O.moe_layer_fast(bits(x), ids.numpy(), w.numpy(), blobs, H, I, K, out_f32=True, y_half=True)
+    assert_close_f32(out.cpu().numpy(), ref32)
 
 
 def _free_port():
