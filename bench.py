@@ -656,10 +656,11 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     X.register()
     T = args.batch
-    if args.only == "prefill":
-        pf = measure_prefill(dev, local, T=args.pf_tokens)
+    if args.only in ("prefill", "ep"):
+        pf = measure_prefill(dev, local, T=args.pf_tokens) if args.only == "prefill" else \
+            measure_prefill_ep(dev, local, world, rank, args.ep_tokens)
         if rank == 0:
-            print(json.dumps({"metric": METRIC, "prefill": pf}), flush=True)
+            print(json.dumps({"metric": METRIC, args.only if args.only == "prefill" else "prefill_ep": pf}), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -884,8 +885,9 @@ def main():
     ap.add_argument("--no-config5", action="store_true", help="skip the configs[4] mixed-bitrate layer")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="configs[3] tokens per batch (8192 or 32768)")
-    ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
-                    help="decode: skip both prefill measurements; prefill: only the configs[2] layer (small profiling runs)")
+    ap.add_argument("--only", choices=["all", "decode", "prefill", "ep"], default="all",
+                    help="decode: skip both prefill measurements; prefill: only the configs[2] layer; ep: only the "
+                         "configs[3] expert-parallel stack (small profiling runs)")
     ap.add_argument("--layers", type=int, default=48, help="decode stack depth (48; fewer only for small profiling runs)")
     ap.add_argument("--slots", type=int, default=8000, help="device cache slots (8000; fewer for small profiling runs)")
     ap.add_argument("--pf-tokens", type=int, default=8192, help="configs[2] prefill tokens")
