@@ -96,6 +96,32 @@ def test_router_logits_bit_exact_tiled(T, H):
     assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("case", ["all_equal", "four_levels", "e64_top32", "e96_top10", "mostly_neg_inf"])
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_router_degenerate_logits(case, T):
+    """Selections the threshold top-k (candidates at or above the top-k-th lane maximum) must get exactly right or
+    hand to the argmax rounds: every logit equal (512 candidates), logits on four levels (ties across lanes), top-32
+    of 64 experts, a small expert count, and five finite logits among -inf (the selection ends in -inf ties)."""
+    H = 2048
+    E, topk = {"e64_top32": (64, 32), "e96_top10": (96, 10)}.get(case, (512, 10))
+    x = synth.activations(T, H, 900 + T)
+    wr = synth.router_weight(E, H, 0.02, 21)
+    bias = None
+    if case in ("all_equal", "four_levels", "mostly_neg_inf"):
+        x = torch.zeros_like(x)   # logits = bias exactly
+        g = torch.Generator().manual_seed(5)
+        bias = {"all_equal": torch.zeros(E),
+                "four_levels": torch.randint(0, 4, (E,), generator=g).float() * 0.5,
+                "mostly_neg_inf": torch.full((E,), float("-inf")).index_put_(
+                    (torch.randperm(E, generator=g)[:5],), torch.randn(5, generator=g))}[case]
+    ids, w = X.router_topk(x.to(DEV), wr.to(DEV), bias.to(DEV) if bias is not None else None, topk)
+    rid, rw, _ = O.router(bits(x), bits(wr), bias.numpy() if bias is not None else None, topk)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    assert np.allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
+    if case == "all_equal":
+        assert np.array_equal(ids.cpu().numpy(), np.tile(np.arange(topk, dtype=np.int32), (T, 1)))
+
+
 @pytest.mark.parametrize("T", [1, 6, 12, 150])
 def test_router_ties_to_lower_id(T):
     """Duplicated router rows give exactly equal logits: the lower expert id is selected first."""
