@@ -160,15 +160,27 @@ __global__ void __launch_bounds__(256) had_in_kernel(PrefillArgs p) {
 // Shared memory per stage: PHASE 0 (gate-up): A[proj][mt] 4 x 16 KB (128 rows x 64 fp16, SW128), B[proj] 2 x 16 KB
 // (128 columns x 64 fp16); PHASE 1 (down): A[mt] 2 x 16 KB, B 32 KB (256 columns x 64 fp16).  After the stages: the
 // mbarriers, the TMEM base slot and the epilogue vectors.
+// Then each decoder warp's ring of trellis words (kWordRing bytes): the words of its 2 column tiles for the next
+// chunks, filled by cp.async several chunks ahead of the decode.
+constexpr int kWordRing = 4096;   // per decoder warp: 4 chunks at K <= 4, 3 at K = 5
+
 template <int PHASE>
 struct GemmCfg {
     static constexpr int NST = PHASE == 0 ? 2 : 3;
     static constexpr int A_BYTES = PHASE == 0 ? 4 * 16384 : 2 * 16384;
     static constexpr int B_BYTES = 32768;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int SMEM = 1024 + NST * STAGE + 1024;
+    static constexpr int SMEM = 1024 + NST * STAGE + 1024 + 8 * kWordRing;
     static constexpr int THREADS = 320;   // warps 0-7 decode + epilogue, warp 8 MMA + TMEM, warp 9 TMA
 };
+static_assert(GemmCfg<0>::SMEM <= 227 * 1024 && GemmCfg<1>::SMEM <= 227 * 1024, "prefill GEMM shared memory");
+
+static __device__ __forceinline__ void pf_cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+static __device__ __forceinline__ void pf_cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+static __device__ __forceinline__ void pf_cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 struct DecCtx {
     const uint32_t* wbase;   // first word of this warp's projection region (row 0)
@@ -177,65 +189,89 @@ struct DecCtx {
     uint32_t sboff;          // byte offset of the warp's first tile inside a stage's B region
 };
 
-// Decoder warp: 2 column tiles x 4 tile rows (64 k) per chunk; words prefetched one chunk ahead in registers.
+// Decoder warp: 2 column tiles x 4 tile rows (64 k) per chunk.  The pair (even ctg, ctg + 1) lies in one PLANAR4
+// group, so per tile row its words are D contiguous plane segments of 2 G words (moe_offload.py:68-73 layout); the
+// warp copies them with cp.async into its word ring NW - 1 chunks ahead, [chunk][tile row][plane][tile][period], and
+// each lane reads its window words from there.
 template <int K, int PHASE>
-__device__ __forceinline__ void decode_loop(const DecCtx& d, uint8_t* sbase, uint64_t* full_b, uint64_t* empty,
-                                            int nchunks) {
+__device__ __forceinline__ void decode_loop(const DecCtx& d, uint8_t* sbase, uint8_t* wring, uint64_t* full_b,
+                                            uint64_t* empty, int nchunks) {
     using C = GemmCfg<PHASE>;
-    constexpr int W = Geo<K>::W, G = Geo<K>::G;
+    constexpr int W = Geo<K>::W, G = Geo<K>::G, D = Geo<K>::D;
+    constexpr int SEGW = 2 * G, ROWW = D * SEGW, CHW = 4 * ROWW;   // words: plane segment, tile row, chunk
+    constexpr int NW = (kWordRing / 4) / CHW >= 4 ? 4 : 3;
+    static_assert(NW * CHW * 4 <= kWordRing && NW >= 3, "decoder word ring");
     const int lane = threadIdx.x & 31;
-    LaneWin<K> lw;
-    lw.init(lane, true);
+    // the lane's window words (plain word w of tile 0: plane w % D, period w / D) in the ring's layout
+    int oA, oB, oC, p0;
+    {
+        constexpr int NB = 256 * K;
+        const int S = (((8 * lane + 1) * K - 16) % NB + NB) % NB;
+        const int w0 = S >> 5;
+        p0 = S & 31;
+        const int wA = w0, wB = (w0 + 1) % (8 * K), wC = (w0 + 2) % (8 * K);
+        oA = (wA % D) * SEGW + wA / D;
+        oB = (wB % D) * SEGW + wB / D;
+        oC = (wC % D) * SEGW + wC / D;
+    }
     const int nl = (lane & 7) + 8 * ((lane >> 3) & 1), kc = (lane >> 4) & 1;
     uint32_t soff[4];
 #pragma unroll
     for (int rr = 0; rr < 4; ++rr) soff[rr] = (uint32_t)nl * 128u + ((uint32_t)((2 * rr + kc) ^ (lane & 7)) << 4);
-    const uint32_t* gp0 = d.wbase + (size_t)(d.ctg >> 2) * 4 * W + (d.ctg & 3) * G;
-    const uint32_t* gp1 = d.wbase + (size_t)((d.ctg + 1) >> 2) * 4 * W + ((d.ctg + 1) & 3) * G;
-    uint32_t wa[8], wb[8], wc[8];
-    auto load = [&](int c) {
+    const uint32_t* gp = d.wbase + (size_t)(d.ctg >> 2) * 4 * W + (d.ctg & 3) * G;   // plane 0 of the pair, row 0
+    const uint32_t wr0 = smem_u32(wring);
+    const uint32_t* wr = reinterpret_cast<const uint32_t*>(wring);
+    auto issue = [&](int c) {
+        if (c < nchunks) {
+            const uint32_t dst0 = wr0 + (uint32_t)((c % NW) * CHW) * 4u;
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const uint32_t* gp = (j ? gp1 : gp0) + (size_t)(c * 4 + rr) * d.row_words;
-                wa[rr * 2 + j] = __ldg(gp + lw.oA);
-                wb[rr * 2 + j] = __ldg(gp + lw.oB);
-                wc[rr * 2 + j] = LaneWin<K>::kNeedC ? __ldg(gp + lw.oC) : 0u;
+            for (int q0 = 0; q0 < CHW / 4; q0 += 32) {
+                const int q = q0 + lane;   // 16-byte piece: tile row, plane, 4-word piece of the segment
+                if (q < CHW / 4) {
+                    const int rr = q / (ROWW / 4), rem = q % (ROWW / 4), i = rem / (SEGW / 4), k4 = rem % (SEGW / 4);
+                    pf_cp_async16(dst0 + (uint32_t)(rr * ROWW + i * SEGW + 4 * k4) * 4u,
+                                  gp + (size_t)(c * 4 + rr) * d.row_words + i * 4 * G + 4 * k4);
+                }
             }
+        }
+        pf_cp_commit();
     };
-    load(0);
+#pragma unroll
+    for (int c = 0; c < NW - 1; ++c) issue(c);
     const uint32_t s0 = smem_u32(sbase) + C::A_BYTES + d.sboff;
 #pragma unroll 1
     for (int c = 0; c < nchunks; ++c) {
         const int s = c % C::NST;
-        uint32_t ca[8], cb[8], cc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { ca[i] = wa[i]; cb[i] = wb[i]; cc[i] = wc[i]; }
-        if (c + 1 < nchunks) load(c + 1);
+        issue(c + NW - 1);
+        pf_cp_wait<NW - 1>();
+        __syncwarp();
+        const uint32_t* cw = wr + (c % NW) * CHW;
         if (c >= C::NST) mbar_wait(&empty[s], (uint32_t)((c / C::NST) - 1) & 1u);
         const uint32_t sb = s0 + (uint32_t)s * C::STAGE;
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
+                const uint32_t* tw = cw + rr * ROWW + j * G;
                 uint32_t f[4];
-                decode8<K>(ca[rr * 2 + j], cb[rr * 2 + j], cc[rr * 2 + j], lw.p0, f);
+                decode8<K>(tw[oA], tw[oB], LaneWin<K>::kNeedC ? tw[oC] : 0u, p0, f);
                 stmatrix_x4(sb + (uint32_t)j * 2048u + soff[rr], f[0], f[1], f[2], f[3]);
             }
         fence_async_smem();
         mbar_arrive(&full_b[s]);
+        __syncwarp();   // every lane has read the ring slot before the next chunk's copies overwrite it
     }
+    pf_cp_wait<0>();
 }
 
 template <int PHASE>
-__device__ __forceinline__ void decode_loop_any(int K, const DecCtx& d, uint8_t* sbase, uint64_t* full_b,
+__device__ __forceinline__ void decode_loop_any(int K, const DecCtx& d, uint8_t* sbase, uint8_t* wring, uint64_t* full_b,
                                                 uint64_t* empty, int nchunks) {
     switch (K) {
-        case 2: decode_loop<2, PHASE>(d, sbase, full_b, empty, nchunks); break;
-        case 3: decode_loop<3, PHASE>(d, sbase, full_b, empty, nchunks); break;
-        case 4: decode_loop<4, PHASE>(d, sbase, full_b, empty, nchunks); break;
-        case 5: decode_loop<5, PHASE>(d, sbase, full_b, empty, nchunks); break;
+        case 2: decode_loop<2, PHASE>(d, sbase, wring, full_b, empty, nchunks); break;
+        case 3: decode_loop<3, PHASE>(d, sbase, wring, full_b, empty, nchunks); break;
+        case 4: decode_loop<4, PHASE>(d, sbase, wring, full_b, empty, nchunks); break;
+        case 5: decode_loop<5, PHASE>(d, sbase, wring, full_b, empty, nchunks); break;
         default:
             // unsupported K (already flagged kErrGeometry): no decode, but the stage hand-over still runs so that
             // no other role of the CTA waits on these warps
@@ -344,7 +380,7 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
             d.ctg = nb * 16 + ctl;
             d.sboff = (uint32_t)ctl * 2048u;
         }
-        decode_loop_any<PHASE>(Kw, d, sbase, full_b, empty, nchunks);
+        decode_loop_any<PHASE>(Kw, d, sbase, tail + 1024 + wid * kWordRing, full_b, empty, nchunks);
     } else if (tid == 8 * 32) {
         // ---- MMA issuer
         const uint32_t idesc = idesc_f16(128, PHASE == 0 ? 128 : 256);
@@ -385,9 +421,23 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
     } else if (tid == 9 * 32) {
         // ---- A producer (TMA)
         const uint32_t bytes = (uint32_t)(PHASE == 0 ? 2 : 1) * (uint32_t)nmt * 16384u;
+        // the stages hold NST chunks; the boxes of the next kPfAhead chunks beyond them are prefetched into L2, so that
+        // a stage's load, issued when the MMA frees it, reads L2 rather than DRAM
+        constexpr int kPfAhead = 3;
+        auto prefetch = [&](int c) {
+            if (c >= nchunks) return;
+            if (PHASE == 0) {
+                for (int q = 0; q < 2; ++q)
+                    for (int mt = 0; mt < nmt; ++mt) tma_prefetch_2d(&tmA, c * 64, q * p.Prow + row0 + mt * 128);
+            } else {
+                for (int mt = 0; mt < nmt; ++mt) tma_prefetch_2d(&tmA, c * 64, row0 + mt * 128);
+            }
+        };
+        for (int c = NST; c < NST + kPfAhead; ++c) prefetch(c);
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
             const int s = c % NST;
+            prefetch(c + NST + kPfAhead);
             if (c >= NST) mbar_wait(&empty[s], (uint32_t)((c / NST) - 1) & 1u);
             uint8_t* sA = sbase + s * C::STAGE;
             mbar_arrive_expect_tx(&full_a[s], bytes);

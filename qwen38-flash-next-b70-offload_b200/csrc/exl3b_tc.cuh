@@ -133,6 +133,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// L2 prefetch of one box of a 2-D tensor map (no shared memory, no barrier; same x alignment rule as tma_load_2d).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
