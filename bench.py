@@ -408,13 +408,14 @@ def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T, cpu_leg=False):
             "config": "configs[2]: 1 layer, 8192 tokens, 512 experts resident, top-10, K=3, logits N(0,1) + bias N(0,1.5)"}
 
 
-def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, warmup=3):
+def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, warmup=3, chunks=2):
     """expert-parallel prefill of the 48-layer stack, T_total tokens per batch split evenly over the ranks
     (strong scaling), the 512 experts sharded contiguously (rank d holds experts [d 512/N, (d+1) 512/N)); NCCL
     all-to-all dispatch and combine around each rank's grouped GEMMs (exl3b200.ep.EPPrefill).  Every layer has its
     own router, bias and inputs; the layers share one synthetic set of 512 experts (915 MB per layer, far above the
     126 MB L2, so sharing the bytes does not change what a layer costs).  Routing is computed before timing.  With
-    one GPU the same stack runs through the single-GPU prefill.  Device time, max over ranks."""
+    one GPU the same stack runs through the single-GPU prefill.  With chunks > 1 each layer's batch is split into
+    that many token ranges whose all-to-alls overlap the other chunks' expert GEMMs.  Device time, max over ranks."""
     import torch
     import torch.distributed as dist
     from exl3b200 import synth
@@ -435,7 +436,7 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
     torch.cuda.synchronize(dev)
     if world > 1:
         from exl3b200.ep import EPPrefill
-        ep = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs_local, max_tokens=T)
+        ep = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs_local, max_tokens=T, chunks=chunks)
         run = lambda li: ep.forward(xs[li], *routes[li])
     else:
         run = lambda li: X.moe_prefill(xs[li], routes[li][0], routes[li][1], ptrs_local, I, K, E)
@@ -460,16 +461,16 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
         ms = float(t[0])
     phases, loads = None, None
     if world > 1:
-        # one more pass with per-phase device events (outside the timed region), and each rank's expert load: the
-        # picks it received over the stack
-        ep.profile = True
+        # one more pass, unchunked, with per-phase device events (outside the timed region), and each rank's expert
+        # load: the picks it received over the stack
+        ep.profile, ep.chunks = True, 1
         acc, picks = {}, 0
         for li in range(layers):
             run(li)
             for kname, v in ep.phase_ms().items():
                 acc[kname] = acc.get(kname, 0.0) + v
             picks += ep.stats()["recv_picks"]
-        ep.profile = False
+        ep.profile, ep.chunks = False, chunks
         t = torch.tensor([acc[kname] for kname in sorted(acc)] + [float(picks)], dtype=torch.float64, device=dev)
         allt = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(allt, t)
@@ -482,7 +483,8 @@ def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, war
            "unit": "tok/s (48-layer stack)", "ms_per_step": round(ms, 3), "n_gpus": world, "scaling": "strong",
            "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world, 1),
            "frac_of_peak_per_gpu": round(flops / (ms * 1e-3) / 1e12 / world / tc, 4),
-           "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if world > 1 else "one GPU",
+           "parallelism": f"expert-parallel x{world} (NCCL all-to-all, {chunks} pipelined chunks per layer)"
+           if world > 1 else "one GPU",
            "phase_us_per_layer_max_over_ranks": phases, "picks_received_per_rank": loads,
            "config": "configs[3]: 48 layers, logits N(0,1) + bias N(0,1.5), top-10, K=3, experts sharded by id"}
     del arena, xs, routes
@@ -658,7 +660,7 @@ def run_ours(args):
     T = args.batch
     if args.only in ("prefill", "ep"):
         pf = measure_prefill(dev, local, T=args.pf_tokens) if args.only == "prefill" else \
-            measure_prefill_ep(dev, local, world, rank, args.ep_tokens)
+            measure_prefill_ep(dev, local, world, rank, args.ep_tokens, chunks=args.ep_chunks)
         if rank == 0:
             print(json.dumps({"metric": METRIC, args.only if args.only == "prefill" else "prefill_ep": pf}), flush=True)
         if world > 1:
@@ -702,7 +704,7 @@ def run_ours(args):
     if not args.no_prefill:
         if world == 1:
             pf = measure_prefill(dev, local, T=args.pf_tokens, cpu_leg=rank == 0 and not args.no_cpu)
-        pf_ep = measure_prefill_ep(dev, local, world, rank, args.ep_tokens)
+        pf_ep = measure_prefill_ep(dev, local, world, rank, args.ep_tokens, chunks=args.ep_chunks)
     hbm, tc, src = peaks()
     distinct = d["distinct"]
     avg_distinct = sum(distinct) / L
@@ -885,6 +887,7 @@ def main():
     ap.add_argument("--no-config5", action="store_true", help="skip the configs[4] mixed-bitrate layer")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="configs[3] tokens per batch (8192 or 32768)")
+    ap.add_argument("--ep-chunks", type=int, default=2, help="configs[3] pipelined token chunks per layer")
     ap.add_argument("--only", choices=["all", "decode", "prefill", "ep"], default="all",
                     help="decode: skip both prefill measurements; prefill: only the configs[2] layer; ep: only the "
                          "configs[3] expert-parallel stack (small profiling runs)")

@@ -12,7 +12,9 @@ of a torch.distributed group (NCCL on B200s):
   counts on the host: a layer queues without a host synchronisation;
 * each rank runs the grouped prefill GEMMs (or the decode kernels for few rows) over all G cap received rows (unused
   rows have no picks and cost nothing) and returns fp16 partial sums per row with a second all-to-all;
-* the source sums a token's partials over the ranks in ascending rank order (exl3b_ep_combine_h), in fp32.
+* the source sums a token's partials over the ranks in ascending rank order (exl3b_ep_combine_h), in fp32;
+* with chunks > 1 the batch is split into that many token ranges, and chunk k + 1's outgoing all-to-all and chunk
+  k - 1's returning one run on NCCL's stream while chunk k's experts run on the compute stream.
 
 Every rank takes the same collective steps in the same order.  The device steps go through the C ABI; `kernels` may
 replace them (the CPU tests use a host implementation of the same contract to run the exchange on gloo ranks).
@@ -89,8 +91,10 @@ class CudaEPKernels:
                                            src.data_ptr(), send.data_ptr(), stream(dev)), "ep_dispatch")
         return {"send": send, "pos": pos, "counts": counts[:G]}
 
-    def combine_h(self, part: torch.Tensor, pos: torch.Tensor, T: int, G: int, H: int, dtype: torch.dtype) -> torch.Tensor:
-        out = torch.empty((T, H), dtype=dtype, device=pos.device)
+    def combine_h(self, part: torch.Tensor, pos: torch.Tensor, T: int, G: int, H: int, dtype: torch.dtype,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty((T, H), dtype=dtype, device=pos.device)
         code = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}[dtype]
         check(_lib.lib().exl3b_ep_combine_h(part.data_ptr() if part.numel() else None, pos.data_ptr(), T, G, H,
                                             out.data_ptr(), out.stride(0), code, stream(pos.device)), "ep_combine_h")
@@ -115,7 +119,7 @@ class EPPrefill:
 
     def __init__(self, group, n_experts: int, H: int, I: int, K: int, ptrs_local: torch.Tensor,
                  kinfo_local: torch.Tensor | None = None, kernels=None, max_tokens: int | None = None,
-                 profile: bool = False):
+                 profile: bool = False, chunks: int = 1):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -129,15 +133,25 @@ class EPPrefill:
         self.k = kernels or CudaEPKernels()
         self.max_tokens = max_tokens
         self.profile = profile
+        if chunks < 1:
+            raise RuntimeError("exl3b200 EPPrefill: chunks must be >= 1")
+        self.chunks = chunks
         self.last = {}
         self._ev = []
 
-    def _a2a(self, out: torch.Tensor, inp: torch.Tensor):
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = False):
         # A peer that stopped (exited, or stuck past the group's timeout) fails the collective; the error names the
         # layer step so that the caller can tell a lost rank from a bad argument.
         try:
-            dist.all_to_all_single(out, inp, group=self.group)
+            return dist.all_to_all_single(out, inp, group=self.group, async_op=async_op)
         except RuntimeError as e:   # torch's distributed backend errors derive from RuntimeError
+            raise RuntimeError(f"exl3b200 EPPrefill: all-to-all failed on rank {self.rank} of {self.G} "
+                               f"(a peer rank stopped or timed out): {e}") from e
+
+    def _wait(self, work):
+        try:
+            work.wait()
+        except RuntimeError as e:
             raise RuntimeError(f"exl3b200 EPPrefill: all-to-all failed on rank {self.rank} of {self.G} "
                                f"(a peer rank stopped or timed out): {e}") from e
 
@@ -174,12 +188,14 @@ class EPPrefill:
         received picks (its expert load)."""
         sc = [int(v) for v in self.last["send_counts"].cpu()]
         idr, cap = self.last["recv_ids"], self.last["cap"]
-        valid = (idr >= 0).any(dim=1).view(self.G, cap)
-        rc = [int(v) for v in valid.sum(dim=1).cpu()]
+        valid = (idr >= 0).any(dim=1).view(-1, self.G, cap)   # [chunk][source rank][record]
+        rc = [int(v) for v in valid.sum(dim=(0, 2)).cpu()]
         return {"cap": cap, "send_counts": sc, "recv_counts": rc, "send_rows": sum(sc), "recv_rows": sum(rc),
                 "recv_picks": int((idr >= 0).sum().item())}
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        if self.chunks > 1:
+            return self._forward_chunked(x, ids, w)
         G, H = self.G, self.H
         T, topk = ids.shape
         dev = x.device
@@ -201,4 +217,44 @@ class EPPrefill:
         out = self.k.combine_h(back, p["pos"], T, G, H, x.dtype)
         self._mark(dev)
         self.last = {"cap": cap, "send_counts": p["counts"], "recv_ids": idr}
+        return out
+
+    def _forward_chunked(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """The same exchange over `chunks` token ranges (each with capacity ceil(cap / chunks)), software-pipelined:
+        the outgoing all-to-all of every chunk is queued on NCCL's stream ahead of the experts, so chunk k + 1's
+        records move while chunk k's experts run, and chunk k's partial sums return while chunk k + 1's run.  The
+        result equals the unchunked forward's (each token's partial sums and their order do not depend on the
+        split)."""
+        G, H, n = self.G, self.H, self.chunks
+        T, topk = ids.shape
+        dev = x.device
+        cap = -(-self._cap(T, dev) // n)
+        bounds = [min(T, k * cap) for k in range(n + 1)]
+        self._ev = []
+        sends, recvs, outs, works = [], [], [], []
+        for k in range(n):
+            a, b = bounds[k], bounds[k + 1]
+            p = self.k.dispatch(x[a:b], ids[a:b], w[a:b], self.E, G, cap)
+            recv = torch.empty_like(p["send"])
+            works.append(self._a2a(recv, p["send"], async_op=True))
+            sends.append(p)
+            recvs.append(recv)
+        backs, bworks, idrs = [], [], []
+        for k in range(n):
+            self._wait(works[k])
+            xr, idr, wr = unpack_records(recvs[k], H, topk, x.dtype)
+            part = self.k.local(xr, idr, wr, self.ptrs_local, self.kinfo_local, self.I, self.K, self.n_local,
+                                dtype=torch.float16)
+            back = torch.empty_like(part)
+            bworks.append(self._a2a(back, part, async_op=True))
+            backs.append(back)
+            idrs.append(idr)
+        out = torch.empty((T, H), dtype=x.dtype, device=dev)
+        for k in range(n):
+            a, b = bounds[k], bounds[k + 1]
+            self._wait(bworks[k])
+            if b > a:
+                self.k.combine_h(backs[k], sends[k]["pos"], b - a, G, H, x.dtype, out=out[a:b])
+        self.last = {"cap": cap, "send_counts": sum(p_["counts"] for p_ in sends),
+                     "recv_ids": torch.cat(idrs), "chunk_caps": [cap] * n}
         return out

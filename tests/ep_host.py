@@ -84,8 +84,12 @@ class HostEPKernels:
             counts[d] = j
         return {"send": torch.from_numpy(send), "pos": torch.from_numpy(pos), "counts": torch.from_numpy(counts)}
 
-    def combine_h(self, part, pos, T, G, H, dtype):
-        return self.combine(part.to(torch.float32), pos, T, G, H, dtype)
+    def combine_h(self, part, pos, T, G, H, dtype, out=None):
+        r = self.combine(part.to(torch.float32), pos, T, G, H, dtype)
+        if out is None:
+            return r
+        out.copy_(r)
+        return out
 
     def combine(self, part, pos, T, G, H, dtype):
         out = torch.zeros((T, H), dtype=torch.float32)

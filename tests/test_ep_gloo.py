@@ -50,7 +50,7 @@ def _worker(rank, world, port, case, q):
         x = synth.activations(T, H, 200 + rank) if T else torch.zeros((0, H), dtype=torch.bfloat16)
         k = HostEPKernels(blobs[rank * per:(rank + 1) * per], H, I, K)
         ep = EPPrefill(dist.group.WORLD, E, H, I, K, torch.zeros(per, dtype=torch.int64), kernels=k,
-                       max_tokens=case.get("max_tokens"))
+                       max_tokens=case.get("max_tokens"), chunks=case.get("chunks", 1))
         out = ep.forward(x, ids, w)
         if T:
             xb = x.view(torch.int16).numpy().view(np.uint16)
@@ -89,6 +89,16 @@ def test_ep_exchange_fixed_capacity():
     last = _run({"T": [7, 5], "max_tokens": 9})
     assert last[0]["cap"] == last[1]["cap"] == 9
     assert [last[d]["recv_counts"][0] for d in range(2)] == last[0]["send_counts"]
+
+
+def test_ep_exchange_in_chunks():
+    """The batch split into 3 token ranges whose exchanges are pipelined with the experts (async all-to-alls): the
+    same outputs, and the per-rank counts add up over the chunks; a rank with fewer tokens than a chunk's capacity
+    sends empty chunks."""
+    last = _run({"T": [7, 2], "chunks": 3})
+    assert last[0]["cap"] == last[1]["cap"] == 3
+    assert [last[d]["recv_counts"][0] for d in range(2)] == last[0]["send_counts"]
+    assert [last[d]["recv_counts"][1] for d in range(2)] == last[1]["send_counts"]
 
 
 def test_ep_rank_without_tokens():

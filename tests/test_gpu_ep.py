@@ -150,6 +150,13 @@ def _nccl_worker(rank, world, port, q):
         one = X2.moe_prefill(x, ids, w, ptrs, I, K, E, out=x32)
         torch.cuda.synchronize()
         close(out.float().cpu().numpy(), one.cpu().numpy(), atol=2e-2, rl2=2e-3)
+        # the batch in 3 pipelined chunks (async all-to-alls on NCCL's stream beside the expert GEMMs): each chunk
+        # runs its experts through the decode kernels or the prefill GEMMs by its own row count
+        ep3 = EPPrefill(dist.group.WORLD, E, H, I, K, ptrs[rank * per:(rank + 1) * per].contiguous(), max_tokens=T,
+                        chunks=3)
+        out3 = ep3.forward(x, ids, w)
+        torch.cuda.synchronize()
+        close(out3.float().cpu().numpy(), one.cpu().numpy(), atol=2e-2, rl2=2e-3)
         q.put((rank, "ok"))
     except Exception as e:
         q.put((rank, f"{type(e).__name__}: {e}"))
