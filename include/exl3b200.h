@@ -133,6 +133,22 @@ int exl3b_moe_decode_cached(const void* x, int64_t x_stride, int x_bf16, int32_t
                             int32_t* ring, int ring_cap, const int32_t* safe, int32_t* vict, uint8_t* vict_ram_res,
                             int H, int I, int K, int E, void* out, int64_t out_stride, int out_bf16, void* workspace,
                             int64_t ws_bytes, int flags, void* stream);
+/* Router + cached decode in one call (no reference counterpart: the reference plugin takes the picks from SGLang's
+ * TopK, plugin/sglang_plugin.tier.py:534-535, and calls moe_forward_cached with them, exl3_moe.a8.sycl:1229-1261).
+ * The same results as exl3b_router_topk (x_bf16, wr_bf16, bias -> ids, w, logits) followed by exl3b_moe_decode_cached
+ * on them: ids / w are written (and rewritten in place for masked picks) as those two calls would.  For small batches
+ * (M <= 8, M topk <= 32) the router kernel writes only the logits and the decode kernels select the picks from them
+ * (one grid completion and the router's last-block arrival fewer per call); larger batches make the two calls.
+ * logits: [M][E] fp32; counter: the router's fused-selection counter (may be NULL), used for larger batches. */
+int exl3b_moe_decode_cached_routed(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias,
+                                   float* logits, int32_t* ids, float* w, int M, int topk, int layer, int64_t* ptrs_all,
+                                   int32_t* slot_of, int32_t* slot_key, int32_t* slot_last, int32_t* tick,
+                                   const int64_t* host_base, int64_t slot_base, int64_t blob, int64_t hstride,
+                                   int64_t* fill_all, int32_t* fill_list, int max_fill, int S, const uint8_t* ram_res,
+                                   int32_t* ring, int ring_cap, const int32_t* safe, int32_t* vict,
+                                   uint8_t* vict_ram_res, int H, int I, int K, int E, void* out, int64_t out_stride,
+                                   int out_bf16, void* workspace, int64_t ws_bytes, int flags, int32_t* counter,
+                                   void* stream);
 /* Profiling hook (no reference counterpart; the reference times graph replays from the host,
  * plugin/sglang_plugin.tier.py:1036-1087): cudaEvent_t handles recorded by exl3b_moe_decode before its route
  * prep, gate-up and down kernels and after down, and by exl3b_moe_prefill before align, before the gate-up GEMM,

@@ -28,6 +28,7 @@
 #include "exl3b_capi_util.h"
 #include "exl3b_ensure.cuh"
 #include "exl3b_launch.h"
+#include "exl3b_topk.cuh"
 #include <algorithm>
 
 namespace exl3b {
@@ -55,7 +56,11 @@ struct DecodeArgs {
     // of ids / w is then done by the last down block
     int small;
     const int32_t* t_slot_of; const uint8_t* t_ram_res; const int32_t* t_safe;
+    // routed small batches (exl3b_moe_decode_cached_routed): the router's logits [M][E]; prep, gate-up and down select
+    // each token's top-k from them themselves (prep also writes ids / w for the caller)
+    const float* logits; int routed;
 };
+
 
 constexpr int kSmallPicks = 32;   // small-batch mode: up to 32 picks (3 tokens at top-10)
 static_assert(kSmallPicks <= kDeferMaskMax, "the cache step defers the tier-mask rewrite of every small batch");
@@ -72,7 +77,16 @@ struct SmallTab {
     unsigned char masked[kSmallPicks];   // tier-masked: becomes (safe, 0)
     unsigned char tok_cnt[kTokPerEnt];
     int n, safe;
+    int rid[kSmallPicks];     // routed: the picks selected in this block
+    float rw[kSmallPicks];
 };
+
+// Routed small batches: warps 0 .. M - 1 select their token's picks into tb.rid / tb.rw (cand: 32 uint2 of scratch
+// shared memory per warp, 8 bytes apart by warp); the caller synchronises the block before group_small reads them.
+__device__ __forceinline__ void routed_select(const DecodeArgs& a, SmallTab& tb, uint2* cand_warp) {
+    const int wid = threadIdx.x >> 5;
+    if (wid < a.M) topk_warp_inl(a.logits, wid, a.E, a.topk, tb.rid, tb.rw, cand_warp);   // row wid of rid / rw
+}
 
 // ------------------------------------------------------------------------------------------------ prep
 // Zero the arrival counters, group active picks by expert (ascending id, picks in ascending index), count active
@@ -342,8 +356,8 @@ __device__ __forceinline__ void group_small(const DecodeArgs& a, SmallTab& tb) {
     // two dependent rounds of L2 loads: (ids, w, safe), then every table entry the pick may need (its own and the
     // safe expert's), selected afterwards
     const int safe = tier ? __ldcg(a.t_safe) : 0;
-    int id = lane < np ? __ldcg(a.ids + lane) : -1;
-    float wv = lane < np ? __ldcg(a.w + lane) : 0.0f;
+    int id = lane < np ? (a.routed ? tb.rid[lane] : __ldcg(a.ids + lane)) : -1;
+    float wv = lane < np ? (a.routed ? tb.rw[lane] : __ldcg(a.w + lane)) : 0.0f;
     const bool safe_ok = tier && safe >= 0 && safe < E;
     const long long p_safe = safe_ok ? (long long)__ldcg(a.ptrs + safe) : 0;
     const int k_safe = (safe_ok && a.kinfo) ? __ldcg(a.kinfo + safe) : kpack;
@@ -397,8 +411,16 @@ __device__ __forceinline__ void group_small(const DecodeArgs& a, SmallTab& tb) {
 // one-warp path first (the other warps zero the arrival counters meanwhile).
 __global__ void __launch_bounds__(1024, 1) prep_kernel(EnsureArgs ea, DecodeArgs da, int cached) {   // 64 registers: no spills
     __shared__ int sh_fast;
+    __shared__ uint2 sh_cand[kTokPerEnt][32];
     pdl_wait();
     pdl_trigger();
+    if (da.routed) {   // the call's picks (the router op's outputs), selected here from the logits
+        const int wid = threadIdx.x >> 5;
+        if (wid < da.M)
+            topk_warp_inl(da.logits, wid, da.E, da.topk, const_cast<int32_t*>(da.ids), const_cast<float*>(da.w),
+                          sh_cand[wid]);   // row wid of ids / w
+        __syncthreads();
+    }
     if (da.M <= kTokPerEnt && da.M * da.topk <= 128 && !(cached && ea.prefetch)) {
         if (threadIdx.x < 32) {
             const bool ok = prep_fast_warp(ea, da, cached);
@@ -944,6 +966,10 @@ __global__ void __launch_bounds__(256, 2) gu_cluster_kernel(DecodeArgs a) {
     if (a.small) {
         // grouping in this CTA: no wait for the prep kernel until the cache fills (below)
         pdl_trigger();
+        if (a.routed) {
+            routed_select(a, *tab, reinterpret_cast<uint2*>(ring));   // the rings are free until the stream starts
+            __syncthreads();
+        }
         if (wid == 0) group_small(a, *tab);
         __syncthreads();
         tb = tab;
@@ -1026,6 +1052,10 @@ __global__ void __launch_bounds__(256, 2) dn_item_kernel(DecodeArgs a) {
     const SmallTab* tb = nullptr;
     int n_ent;
     if (a.small) {   // own grouping, as the gate-up kernel
+        if (a.routed) {
+            routed_select(a, *tab, reinterpret_cast<uint2*>(ring));
+            __syncthreads();
+        }
         if (wid == 0) group_small(a, *tab);
         __syncthreads();
         tb = tab;
@@ -1245,6 +1275,7 @@ static int run_decode(DecodeArgs& a, const EnsureArgs* ea, void* workspace, int6
     a.blocks_done = (int*)(b + L.off[kWsBlocksDone]);
     a.maxent = M * topk;
     a.small = (M <= kTokPerEnt && M * topk <= kSmallPicks && !(ea && ea->prefetch)) ? 1 : 0;
+    EXL3B_CHECK(!a.routed || a.small, "exl3b_moe_decode_cached_routed: in-kernel selection is for small batches only");
     EnsureArgs none{};
     prof_record(0, s);
     cudaError_t e = launch_k(prep_kernel, dim3(1), dim3(1024), 0, s, ea ? *ea : none, a, ea ? 1 : 0);
@@ -1321,15 +1352,19 @@ extern "C" EXL3B_API int exl3b_moe_decode(const void* x, int64_t x_stride, int x
     return run_decode(a, nullptr, workspace, ws_bytes, (cudaStream_t)stream, nullptr, nullptr, 0, 0, nullptr, 0);
 }
 
-extern "C" EXL3B_API int exl3b_moe_decode_cached(const void* x, int64_t x_stride, int x_bf16, int32_t* ids, float* w, int M,
-                                                 int topk, int layer, int64_t* ptrs_all, int32_t* slot_of,
-                                                 int32_t* slot_key, int32_t* slot_last, int32_t* tick,
-                                                 const int64_t* host_base, int64_t slot_base, int64_t blob, int64_t hstride,
-                                                 int64_t* fill_all, int32_t* fill_list, int max_fill, int S,
-                                                 const uint8_t* ram_res, int32_t* ring, int ring_cap, const int32_t* safe,
-                                                 int32_t* vict, uint8_t* vict_ram_res, int H, int I, int K, int E,
-                                                 void* out, int64_t out_stride, int out_bf16, void* workspace,
-                                                 int64_t ws_bytes, int flags, void* stream) {
+namespace exl3b {
+int router_logits_launch(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias, int T, int H,
+                         int E, float* logits, cudaStream_t s);
+}
+
+// Cached decode; with logits set (routed entry, small batches) the kernels select the picks from them.
+static int decode_cached_impl(const void* x, int64_t x_stride, int x_bf16, int32_t* ids, float* w, int M, int topk,
+                              int layer, int64_t* ptrs_all, int32_t* slot_of, int32_t* slot_key, int32_t* slot_last,
+                              int32_t* tick, const int64_t* host_base, int64_t slot_base, int64_t blob, int64_t hstride,
+                              int64_t* fill_all, int32_t* fill_list, int max_fill, int S, const uint8_t* ram_res,
+                              int32_t* ring, int ring_cap, const int32_t* safe, int32_t* vict, uint8_t* vict_ram_res,
+                              int H, int I, int K, int E, void* out, int64_t out_stride, int out_bf16, void* workspace,
+                              int64_t ws_bytes, int flags, void* stream, const float* logits) {
     int rc = check_args(x, x_stride, ids, w, M, topk, ptrs_all, nullptr, H, I, K, E, out, out_stride, out_bf16);
     if (rc) return rc;
     EXL3B_CHECK(layer >= 0 && S > 0 && slot_of && slot_key && slot_last && tick && host_base && fill_all && fill_list,
@@ -1345,6 +1380,8 @@ extern "C" EXL3B_API int exl3b_moe_decode_cached(const void* x, int64_t x_stride
     a.fill_list = fill_list;
     a.fill = fill_all + (int64_t)layer * E;
     a.blob = blob;
+    a.logits = logits;
+    a.routed = logits ? 1 : 0;
     int mf = max_fill < E ? max_fill : E;
     EnsureArgs ea{ids, w, M * topk, layer, E, S, ptrs_all, slot_of, slot_key, slot_last, tick, host_base, slot_base, blob,
                   hstride > 0 ? hstride : blob, fill_all, fill_list, mf, 0, nullptr, ram_res, ring, ring_cap, safe, vict};
@@ -1356,6 +1393,61 @@ extern "C" EXL3B_API int exl3b_moe_decode_cached(const void* x, int64_t x_stride
     int nvict = vict ? std::min(mf, M * topk) : 0;
     return run_decode(a, &ea, workspace, ws_bytes, (cudaStream_t)stream, vict, host_base, slot_base,
                       hstride > 0 ? hstride : blob, vict_ram_res, nvict);
+}
+
+extern "C" EXL3B_API int exl3b_moe_decode_cached(const void* x, int64_t x_stride, int x_bf16, int32_t* ids, float* w, int M,
+                                                 int topk, int layer, int64_t* ptrs_all, int32_t* slot_of,
+                                                 int32_t* slot_key, int32_t* slot_last, int32_t* tick,
+                                                 const int64_t* host_base, int64_t slot_base, int64_t blob, int64_t hstride,
+                                                 int64_t* fill_all, int32_t* fill_list, int max_fill, int S,
+                                                 const uint8_t* ram_res, int32_t* ring, int ring_cap, const int32_t* safe,
+                                                 int32_t* vict, uint8_t* vict_ram_res, int H, int I, int K, int E,
+                                                 void* out, int64_t out_stride, int out_bf16, void* workspace,
+                                                 int64_t ws_bytes, int flags, void* stream) {
+    return decode_cached_impl(x, x_stride, x_bf16, ids, w, M, topk, layer, ptrs_all, slot_of, slot_key, slot_last, tick,
+                              host_base, slot_base, blob, hstride, fill_all, fill_list, max_fill, S, ram_res, ring,
+                              ring_cap, safe, vict, vict_ram_res, H, I, K, E, out, out_stride, out_bf16, workspace,
+                              ws_bytes, flags, stream, nullptr);
+}
+
+extern "C" int exl3b_router_topk(const void* x_bf16, int64_t x_stride, const void* wr_bf16, const float* bias, int T,
+                                 int H, int E, int topk, int32_t* ids, float* w, float* logits, int32_t* counter,
+                                 void* stream);
+
+extern "C" EXL3B_API int exl3b_moe_decode_cached_routed(const void* x_bf16, int64_t x_stride, const void* wr_bf16,
+                                                        const float* bias, float* logits, int32_t* ids, float* w, int M,
+                                                        int topk, int layer, int64_t* ptrs_all, int32_t* slot_of,
+                                                        int32_t* slot_key, int32_t* slot_last, int32_t* tick,
+                                                        const int64_t* host_base, int64_t slot_base, int64_t blob,
+                                                        int64_t hstride, int64_t* fill_all, int32_t* fill_list,
+                                                        int max_fill, int S, const uint8_t* ram_res, int32_t* ring,
+                                                        int ring_cap, const int32_t* safe, int32_t* vict,
+                                                        uint8_t* vict_ram_res, int H, int I, int K, int E, void* out,
+                                                        int64_t out_stride, int out_bf16, void* workspace,
+                                                        int64_t ws_bytes, int flags, int32_t* counter, void* stream) {
+    EXL3B_CHECK(x_bf16 && wr_bf16 && logits && ids && w, "exl3b_moe_decode_cached_routed: null pointer");
+    EXL3B_CHECK(topk >= 1 && topk <= 32 && topk <= E, "exl3b_moe_decode_cached_routed: 1 <= topk <= min(32, E)");
+    if (M == 0) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (M <= kTokPerEnt && M * topk <= kSmallPicks) {
+        // small batch: logits only, the decode kernels select (prep writes ids / w)
+        EXL3B_CHECK(H % 256 == 0 && H <= 4096 && x_stride >= H && ((x_stride * 2) % 16) == 0 &&
+                        (((uintptr_t)x_bf16) & 15) == 0 && (((uintptr_t)wr_bf16) & 15) == 0,
+                    "exl3b_moe_decode_cached_routed: router operand shape / alignment");
+        int rc = router_logits_launch(x_bf16, x_stride, wr_bf16, bias, M, H, E, logits, s);
+        if (rc) return rc;
+        return decode_cached_impl(x_bf16, x_stride, 1, ids, w, M, topk, layer, ptrs_all, slot_of, slot_key, slot_last,
+                                  tick, host_base, slot_base, blob, hstride, fill_all, fill_list, max_fill, S, ram_res,
+                                  ring, ring_cap, safe, vict, vict_ram_res, H, I, K, E, out, out_stride, out_bf16,
+                                  workspace, ws_bytes, flags, stream, logits);
+    }
+    // larger batches: the router op, then the cached decode
+    int rc = exl3b_router_topk(x_bf16, x_stride, wr_bf16, bias, M, H, E, topk, ids, w, logits, counter, stream);
+    if (rc) return rc;
+    return decode_cached_impl(x_bf16, x_stride, 1, ids, w, M, topk, layer, ptrs_all, slot_of, slot_key, slot_last, tick,
+                              host_base, slot_base, blob, hstride, fill_all, fill_list, max_fill, S, ram_res, ring,
+                              ring_cap, safe, vict, vict_ram_res, H, I, K, E, out, out_stride, out_bf16, workspace,
+                              ws_bytes, flags, stream, nullptr);
 }
 
 extern "C" EXL3B_API int exl3b_set_profile_events(void* before_route, void* before_gateup, void* before_down,

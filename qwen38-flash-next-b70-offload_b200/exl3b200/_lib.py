@@ -44,6 +44,9 @@ _SIGS = {
     "exl3b_set_profile_events": (ci, [vp, vp, vp, vp]),
     "exl3b_moe_decode_cached": (ci, [vp, i64, ci, vp, vp, ci, ci, ci, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, ci, ci,
                                      vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, vp, i64, ci, vp, i64, ci, vp]),
+    "exl3b_moe_decode_cached_routed": (ci, [vp, i64, vp, vp, vp, vp, vp, ci, ci, ci, vp, vp, vp, vp, vp, vp, i64, i64,
+                                            i64, vp, vp, ci, ci, vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, vp, i64, ci, vp,
+                                            i64, ci, vp, vp]),
     "exl3b_align_scratch": (i64, [ci, ci]),
     "exl3b_align": (ci, [vp, vp, ci, ci, ci, ci, vp, vp, ci, ci, vp, i64, vp]),
     "exl3b_ep_plan": (ci, [vp, vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),

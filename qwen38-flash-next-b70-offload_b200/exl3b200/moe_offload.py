@@ -346,6 +346,18 @@ class ExpertStore:
             return _ops._moe_forward_cached_impl(*args, out=out)
         return self.X.moe_forward_cached(*args)
 
+    def forward_cached_routed(self, key, x: torch.Tensor, wr: torch.Tensor, bias: torch.Tensor | None, topk: int,
+                              max_fill: int | None = None, out: torch.Tensor | None = None):
+        """The router (logits x Wr^T + bias, softmax top-k) and forward_cached on its picks in one call (this build's
+        extension: the reference plugin takes its picks from SGLang's TopK).  Returns (out, topk_ids, topk_w) with the
+        values router_topk + forward_cached give, ids / w after the tier mask's rewrite; small batches select the
+        picks inside the decode kernels, one grid completion fewer per call."""
+        self._cache_used = True
+        return _ops._moe_forward_cached_routed_impl(
+            x, wr, bias, topk, self.ptrs_all, self.layer_index[key], self.slot_of_dev, self.slot_key, self.slot_last,
+            self.tick, self.host_base, self.slot_base, self.fill_all, self.fill_list,
+            self.E if max_fill is None else max_fill, self.I, self.K, self.E, self.pend, self.done_seq, out=out)
+
     def prefetch(self, key, ids: torch.Tensor, max_fill: int = 16) -> None:
         """Claim LRU slots for the predicted experts `ids` of `key` and copy them from host, on the CURRENT stream
         (a side stream that waited for the previous MoE call; the compute stream waits for it before the next).  The

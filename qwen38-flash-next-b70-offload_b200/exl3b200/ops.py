@@ -254,6 +254,52 @@ def _moe_forward_cached_impl(x, topk_ids, topk_w, ptrs_all, layer, slot_of, slot
     return out
 
 
+def _moe_forward_cached_routed_impl(x, wr, bias, topk, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
+                                    slot_base, fill_all, fill_list, max_fill, I, K, n_experts, pend, done_seq, out=None):
+    """router_topk(x, wr, bias, topk) followed by the cached decode on its picks, as one call: returns (out, ids, w),
+    the same values the two calls give.  Small batches select the picks inside the decode kernels."""
+    if x.dtype != torch.bfloat16 or wr.dtype != torch.bfloat16:
+        raise RuntimeError("exl3b200 moe_forward_cached_routed: x and Wr must be bf16")
+    if x.dim() != 2 or x.stride(1) != 1 or not wr.is_contiguous():
+        raise RuntimeError("exl3b200 moe_forward_cached_routed: x 2-D unit-stride rows, Wr contiguous")
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise RuntimeError("exl3b200 moe_forward_cached_routed: bias must be contiguous fp32")
+    E = n_experts
+    M, H = x.shape
+    if wr.shape[0] != E:
+        raise RuntimeError("exl3b200 moe_forward_cached_routed: Wr must have n_experts rows")
+    if M == 0 or M >= G.prefill_min_m or slot_key.numel() == 0 or (pend.numel() and done_seq.numel()):
+        ids, w = router_topk(x, wr, bias, topk)
+        y = _moe_forward_cached_impl(x, ids, w, ptrs_all, layer, slot_of, slot_key, slot_last, tick, host_base,
+                                     slot_base, fill_all, fill_list, max_fill, I, K, E, pend, done_seq, out=out)
+        return y, ids, w
+    if ptrs_all.dtype != torch.int64 or fill_all.dtype != torch.int64 or slot_of.dtype != torch.int32:
+        raise RuntimeError("exl3b200 moe_forward_cached_routed: int64 ptrs_all / fill_all, int32 slot_of")
+    blob = blob_bytes(H, I, K)
+    S = slot_key.numel()
+    if out is None:
+        out = torch.empty_like(x)
+    ids = torch.empty((M, topk), dtype=torch.int32, device=x.device)
+    w = torch.empty((M, topk), dtype=torch.float32, device=x.device)
+    logits = torch.empty((M, E), dtype=torch.float32, device=x.device)
+    L = _lib.lib()
+    wsb = int(L.exl3b_moe_decode_workspace(M, topk, H, I))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
+    rr = G.ram_res
+    vict = G.vict
+    if vict is not None and G.vring is not None and G.vring[1].numel() < min(max_fill, E):
+        raise RuntimeError("exl3b200 moe_forward_cached: the victim ring's sel needs one entry per possible victim")
+    check(L.exl3b_moe_decode_cached_routed(
+        x.data_ptr(), x.stride(0), wr.data_ptr(), ptr(bias), logits.data_ptr(), ids.data_ptr(), w.data_ptr(), M, topk,
+        layer, ptrs_all.data_ptr(), slot_of.data_ptr(), slot_key.data_ptr(), slot_last.data_ptr(), tick.data_ptr(),
+        host_base.data_ptr(), slot_base, blob, G.host_stride or blob, fill_all.data_ptr(), fill_list.data_ptr(),
+        min(max_fill, E), S, ptr(rr), ptr(G.ring if rr is not None else None),
+        (G.ring.numel() - 1) if rr is not None else 0, ptr(G.safe if rr is not None else None), ptr(vict), ptr(rr),
+        H, I, K, E, out.data_ptr(), out.stride(0), _OUT_CODE[out.dtype], ws.data_ptr(), wsb,
+        1 if G.skip_zero else 0, _router_counter(x.device), stream(x.device)), "moe_forward_cached_routed")
+    return out, ids, w
+
+
 def tier_prefetch_ids(ids, layer, n_experts, slot_of, ram_res, safe):
     """With the RAM tier on, a predicted expert that is in neither VRAM nor RAM has no valid host row to copy from (its
     row may have been released): it is replaced by the layer's safe expert, which is always resident.  Device ops
