@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // One warp per expert, 8 experts per block; blockIdx.y = token chunk of TC tokens.  Lane c owns chunk c:
 // its slice of Wr[e] stays in registers across the chunk's tokens.
 template <int CL, int TC>
-__global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
+__global__ void __launch_bounds__(256, 2) router_logits_kernel(const __nv_bfloat16* __restrict__ x, long long xs,
                                                             const __nv_bfloat16* __restrict__ wr,
                                                             const float* __restrict__ bias, int T, int H, int E,
                                                             float* __restrict__ logits, int topk, int* __restrict__ ids,
