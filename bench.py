@@ -413,7 +413,7 @@ def measure_prefill(dev, local, iters=10, warmup=3, T=PF_T, cpu_leg=False):
             "config": "configs[2]: 1 layer, 8192 tokens, 512 experts resident, top-10, K=3, logits N(0,1) + bias N(0,1.5)"}
 
 
-def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, warmup=3, chunks=2):
+def measure_prefill_ep(dev, local, world, rank, T_total, layers=48, iters=3, warmup=3, chunks=1):
     """expert-parallel prefill of the 48-layer stack, T_total tokens per batch split evenly over the ranks
     (strong scaling), the 512 experts sharded contiguously (rank d holds experts [d 512/N, (d+1) 512/N)); NCCL
     all-to-all dispatch and combine around each rank's grouped GEMMs (exl3b200.ep.EPPrefill).  Every layer has its
@@ -900,7 +900,7 @@ def main():
     ap.add_argument("--no-config5", action="store_true", help="skip the configs[4] mixed-bitrate layer")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="configs[3] tokens per batch (8192 or 32768)")
-    ap.add_argument("--ep-chunks", type=int, default=2, help="configs[3] pipelined token chunks per layer")
+    ap.add_argument("--ep-chunks", type=int, default=1, help="configs[3] pipelined token chunks per layer")
     ap.add_argument("--only", choices=["all", "decode", "prefill", "ep"], default="all",
                     help="decode: skip both prefill measurements; prefill: only the configs[2] layer; ep: only the "
                          "configs[3] expert-parallel stack (small profiling runs)")
