@@ -41,6 +41,21 @@ def test_blob_bytes_and_abi():
     assert L.exl3b_moe_decode_workspace(1, 10, 2048, 768) > 0
 
 
+def _routed_args(logits=1 << 20, topk=10, H=2048):
+    """exl3b_moe_decode_cached_routed arguments for one token (valid pointers as placeholders; nothing launches
+    because each case fails a check first)."""
+    p = 1 << 20
+    return [p, H, p, None, logits, p, p, 1, topk, 0, p, p, p, p, p, p, 0, 1786368, 0, p, p, 8, 8000, None, None, 0,
+            None, None, None, H, 768, 3, 512, p, H, 1, p, 1 << 30, 1, None, None]
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.exl3b_moe_decode_workspace(0, 10, 2048, 768) == 0,
+])
+def test_degenerate_sizes(call):
+    assert call(_lib.lib())
+
+
 @pytest.mark.parametrize("call", [
     lambda L: L.exl3b_dequant(None, 1, 24, 0, 4, 3, 1, None, 64, None),
     lambda L: L.exl3b_dequant(1 << 20, 1, 24, 1, 4, 3, 1, 1 << 21, 64, None),      # planar tile0 % 4
@@ -59,6 +74,14 @@ def test_blob_bytes_and_abi():
                                   [1 << 20] * 4 + [2, None])),                      # layer outside the plan buffer
     lambda L: L.exl3b_cepf_commit(None, 1 << 20, 2, 512, 8, 1 << 20, 1 << 20, 0, 64, None),
     lambda L: L.exl3b_cepf_worker_start(1 << 20, 0, 512, 8, 1 << 20, 0, 64, 64, 1 << 20, 0, None),   # no layers
+    lambda L: L.exl3b_moe_decode_cached_routed(*_routed_args(logits=None)),                          # no logits
+    lambda L: L.exl3b_moe_decode_cached_routed(*_routed_args(topk=40)),                              # topk > 32
+    lambda L: L.exl3b_moe_decode_cached_routed(*_routed_args(H=2000)),                               # router H
+    lambda L: L.exl3b_ep_dispatch(1 << 20, 2048, 1 << 20, 1 << 20, 8, 10, 512, 3, 2048, 8, 1 << 20, 1 << 20,
+                                  1 << 20, 1 << 20, 1 << 20, None),                 # E % G
+    lambda L: L.exl3b_ep_dispatch(1 << 20, 2048, 1 << 20, 1 << 20, 8, 10, 512, 2, 2048, 4, 1 << 20, 1 << 20,
+                                  1 << 20, 1 << 20, 1 << 20, None),                 # cap < T
+    lambda L: L.exl3b_ep_combine_h(1 << 20, 1 << 20, 4, 2, 2046, 1 << 20, 2048, 0, None),   # H % 4
 ])
 def test_invalid_arguments_rejected_before_launch(call):
     L = _lib.lib()
