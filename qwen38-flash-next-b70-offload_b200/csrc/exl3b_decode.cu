@@ -737,15 +737,17 @@ __device__ __forceinline__ void dn_token_epilogue(const DecodeArgs& a, int ent, 
     yv.z = v[2] * (kRsqrt128 * wt) * __half2float(svd[2]);
     yv.w = v[3] * (kRsqrt128 * wt) * __half2float(svd[3]);
     __stcg(reinterpret_cast<float4*>(a.y + (size_t)pick * a.H + nbh * 128 + 4 * lane), yv);
+    // the warp barrier orders every lane's y store before lane 0's release; for the last arrival, lane 0's acquire
+    // and the warp barrier after it make the other picks' rows visible to every lane
     __syncwarp();
-    __threadfence();
     const int mt = pick / a.topk;
     int oc = 0;
-    if (lane == 0) oc = atomicAdd(&a.cnt_c[mt * nbH + nbh], 1);
+    if (lane == 0)
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(oc) : "l"(&a.cnt_c[mt * nbH + nbh]) : "memory");
     oc = __shfl_sync(0xffffffffu, oc, 0);
+    __syncwarp();
     const int tcnt = tb ? (int)tb->tok_cnt[mt] : __ldcg(a.tok_cnt + mt);
     if (oc == tcnt - 1) {
-        __threadfence();
         // up to 12 picks' rows and flags loaded at once (one round trip), then summed in pick order; rows of
         // inactive picks (in bounds, never written this call) are loaded and skipped
         constexpr int kComb = 12;

@@ -79,15 +79,16 @@ __global__ void __launch_bounds__(256, 2) router_logits_kernel(const __nv_bfloat
     }
     if (!counter) return;
     // fused selection: the last block to finish runs the top-k of every token (T <= 8, one warp per token)
+    // the block barrier orders every warp's logits before thread 0's release; the last block's acquire, then its
+    // barrier, make every block's logits visible to all of its threads
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        int old = atomicAdd(counter, 1);
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(old) : "l"(counter) : "memory");
         sh_last = old == (int)(gridDim.x * gridDim.y) - 1;
     }
     __syncthreads();
     if (!sh_last) return;
-    __threadfence();
     int t = threadIdx.x >> 5;
     if (t < T) topk_warp(logits, t, E, topk, ids, w, cand[t]);
     if (threadIdx.x == 0) *counter = 0;
