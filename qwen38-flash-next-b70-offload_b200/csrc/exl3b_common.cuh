@@ -148,26 +148,59 @@ __device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], uint32
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// ------------------------------------------------------------------------------------------------ packed fp32
+// sm_100 issues two fp32 adds, multiplies or FMAs of a float2 as one instruction; each component rounds exactly as
+// the scalar operation does.  a - b is formed as fma(b, -1, a): b * -1 is exact, so the single rounding is that of
+// a - b.
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    float2 r;
+    asm("{\n .reg .b64 pa, pb, pd;\n mov.b64 pa, {%2, %3};\n mov.b64 pb, {%4, %5};\n"
+        " add.rn.f32x2 pd, pa, pb;\n mov.b64 {%0, %1}, pd;\n}\n"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    float2 r;
+    asm("{\n .reg .b64 pa, pb, pd;\n mov.b64 pa, {%2, %3};\n mov.b64 pb, {%4, %5};\n"
+        " mul.rn.f32x2 pd, pa, pb;\n mov.b64 {%0, %1}, pd;\n}\n"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{\n .reg .b64 pa, pb, pc, pd;\n mov.b64 pa, {%2, %3};\n mov.b64 pb, {%4, %5};\n mov.b64 pc, {%6, %7};\n"
+        " fma.rn.f32x2 pd, pa, pb, pc;\n mov.b64 {%0, %1}, pd;\n}\n"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) { return f2_fma(b, make_float2(-1.0f, -1.0f), a); }
+
 // ------------------------------------------------------------------------------------------------ FWHT
 // In-warp FWHT-128 of one row held as 4 consecutive values per lane (v[j] = element 4*lane + j), Sylvester order,
 // unnormalised, fp32 butterflies with strides 1, 2, 4, ..., 64 (exl3_esimd.h:210-221): strides 1 and 2 are inside
-// the lane, strides 4..64 pair lanes lane ^ (stride/4).  Each butterfly computes a+b / a-b exactly as the reference.
+// the lane, strides 4..64 pair lanes lane ^ (stride/4).  Each butterfly computes a+b / a-b exactly as the reference;
+// stride 2 and the cross-lane strides run on float2 pairs (v0, v1), (v2, v3).
 __device__ __forceinline__ void fwht128_warp(float v[4], int lane) {
     float a, b;
     a = v[0]; b = v[1]; v[0] = a + b; v[1] = a - b;
     a = v[2]; b = v[3]; v[2] = a + b; v[3] = a - b;
-    a = v[0]; b = v[2]; v[0] = a + b; v[2] = a - b;
-    a = v[1]; b = v[3]; v[1] = a + b; v[3] = a - b;
+    float2 p = make_float2(v[0], v[1]), q = make_float2(v[2], v[3]);
+    {
+        const float2 s = f2_add(p, q), d = f2_sub(p, q);
+        p = s; q = d;
+    }
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        bool upper = (lane & m) != 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float o = __shfl_xor_sync(0xffffffffu, v[j], m);
-            // lower element (lane without bit m) holds a, upper holds b: lower gets a + b, upper gets a - b
-            v[j] = upper ? (o - v[j]) : (v[j] + o);
-        }
+        // lower element (lane without bit m) holds a, upper holds b: lower gets a + b = o + v, upper gets a - b =
+        // o - v, i.e. fma(v, sign, o) with sign = -1 on the upper lane (v * -1 is exact)
+        const float sg = (lane & m) ? -1.0f : 1.0f;
+        const float2 sg2 = make_float2(sg, sg);
+        const float2 op = make_float2(__shfl_xor_sync(0xffffffffu, p.x, m), __shfl_xor_sync(0xffffffffu, p.y, m));
+        const float2 oq = make_float2(__shfl_xor_sync(0xffffffffu, q.x, m), __shfl_xor_sync(0xffffffffu, q.y, m));
+        p = f2_fma(p, sg2, op);
+        q = f2_fma(q, sg2, oq);
     }
+    v[0] = p.x; v[1] = p.y; v[2] = q.x; v[3] = q.y;
 }
 
 __device__ __forceinline__ float rn16(float f) { return __half2float(__float2half_rn(f)); }

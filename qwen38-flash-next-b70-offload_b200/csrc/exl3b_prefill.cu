@@ -290,17 +290,35 @@ __device__ __forceinline__ void tmem_row128(uint32_t taddr, float v[128]) {
     for (int q = 0; q < 4; ++q) tmem_ld32(taddr + q * 32, v + q * 32);
 }
 
+// One butterfly stage of stride HS >= 2 over a row of 128 registers: the pairs (j, j + 1) and (j + HS, j + HS + 1)
+// as float2s (32 packed additions and 32 packed subtractions).
+template <int HS>
+__device__ __forceinline__ void fwht128_stage2(float v[128]) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+        const int j = (t / (HS / 2)) * (2 * HS) + (t % (HS / 2)) * 2;
+        const float2 a = make_float2(v[j], v[j + 1]), b = make_float2(v[j + HS], v[j + HS + 1]);
+        const float2 sm = f2_add(a, b), df = f2_sub(a, b);
+        v[j] = sm.x; v[j + 1] = sm.y;
+        v[j + HS] = df.x; v[j + HS + 1] = df.y;
+    }
+}
+
+// FWHT-128 of one row in registers, strides 1, 2, ..., 64 in that order (a + b / a - b per butterfly).  Stride 1
+// pairs the two halves of a float2 and runs scalar; strides 2..64 run on float2 pairs with the same roundings.
 __device__ __forceinline__ void fwht128_regs(float v[128]) {
 #pragma unroll
-    for (int h = 1; h < 128; h <<= 1)
-#pragma unroll
-        for (int i = 0; i < 128; i += 2 * h)
-#pragma unroll
-            for (int j = i; j < i + h; ++j) {
-                float a = v[j], b = v[j + h];
-                v[j] = a + b;
-                v[j + h] = a - b;
-            }
+    for (int j = 0; j < 128; j += 2) {
+        const float a = v[j], b = v[j + 1];
+        v[j] = a + b;
+        v[j + 1] = a - b;
+    }
+    fwht128_stage2<2>(v);
+    fwht128_stage2<4>(v);
+    fwht128_stage2<8>(v);
+    fwht128_stage2<16>(v);
+    fwht128_stage2<32>(v);
+    fwht128_stage2<64>(v);
 }
 
 template <int PHASE>
@@ -494,8 +512,9 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
 #pragma unroll
                         for (int jj = 0; jj < 4; ++jj) {
                             const int j = q * 8 + 2 * jj;
-                            __half2 h = __floats2half2_rn(v[j] * kRsqrt128 * __half2float(sv[j]),
-                                                          v[j + 1] * kRsqrt128 * __half2float(sv[j + 1]));
+                            const float2 t = f2_mul(f2_mul(make_float2(v[j], v[j + 1]), make_float2(kRsqrt128, kRsqrt128)),
+                                                    __half22float2(*reinterpret_cast<const __half2*>(sv + j)));
+                            __half2 h = __float22half2_rn(t);
                             ow[jj] = *reinterpret_cast<uint32_t*>(&h);
                         }
                         *reinterpret_cast<uint4*>(st + ((q ^ (tid & 15)) << 4)) = o;
@@ -508,7 +527,8 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
                         uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
                         for (int jj = 0; jj < 4; ++jj) {
-                            __half2 h = __floats2half2_rn(v[q * 8 + 2 * jj] * kRsqrt128, v[q * 8 + 2 * jj + 1] * kRsqrt128);
+                            __half2 h = __float22half2_rn(f2_mul(make_float2(v[q * 8 + 2 * jj], v[q * 8 + 2 * jj + 1]),
+                                                                 make_float2(kRsqrt128, kRsqrt128)));
                             ow[jj] = *reinterpret_cast<uint32_t*>(&h);
                         }
                         op[q] = o;
@@ -542,6 +562,7 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
             }
         } else {
             const float wt = valid ? p.pair_w[pr] : 0.0f;
+            const float2 rw2 = make_float2(kRsqrt128 * wt, kRsqrt128 * wt);
 #pragma unroll 1
             for (int hb = 0; hb < 2; ++hb) {
                 tmem_row128(tl + (uint32_t)(mt * 256 + hb * 128), v);
@@ -555,9 +576,9 @@ __global__ void __launch_bounds__(320, 1) prefill_gemm_kernel(PrefillArgs p, con
 #pragma unroll
                         for (int jj = 0; jj < 4; ++jj) {
                             const int c0 = hb * 128 + q * 8 + 2 * jj;
-                            float y0 = v[q * 8 + 2 * jj] * (kRsqrt128 * wt) * __half2float(vec[c0]);
-                            float y1 = v[q * 8 + 2 * jj + 1] * (kRsqrt128 * wt) * __half2float(vec[c0 + 1]);
-                            __half2 h = __floats2half2_rn(y0, y1);
+                            const float2 t = f2_mul(f2_mul(make_float2(v[q * 8 + 2 * jj], v[q * 8 + 2 * jj + 1]), rw2),
+                                                    __half22float2(*reinterpret_cast<const __half2*>(vec + c0)));
+                            __half2 h = __float22half2_rn(t);
                             ow[jj] = *reinterpret_cast<uint32_t*>(&h);
                         }
                         op[q] = o;
