@@ -38,10 +38,19 @@ __global__ void __launch_bounds__(kAlignBlock) align_scan_kernel(int* __restrict
     const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
     int c = 0;
     if (e < E) {
-        for (int b = 0; b < nblk; ++b) {   // per-block offsets inside the expert (exclusive over blocks)
-            int v = bc[(size_t)b * E + e];
-            bc[(size_t)b * E + e] = c;
-            c += v;
+        // per-block offsets inside the expert (exclusive over blocks); the counts are read 16 blocks at a time so
+        // that one L2 round trip covers 16 of them
+        constexpr int kB = 16;
+        for (int b0 = 0; b0 < nblk; b0 += kB) {
+            int v[kB];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) v[j] = b0 + j < nblk ? bc[(size_t)(b0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < kB; ++j)
+                if (b0 + j < nblk) {
+                    bc[(size_t)(b0 + j) * E + e] = c;
+                    c += v[j];
+                }
         }
     }
     int pc = (c + pad - 1) / pad * pad;
@@ -97,11 +106,14 @@ __global__ void __launch_bounds__(kAlignBlock) align_place_kernel(const int32_t*
     int rank = __popc(peers & ((1u << lane) - 1u));
     int leader_last = 31 - __clz(peers);   // highest lane of the group updates the running count
     if (i < P && !ok) o.pair_of[i] = -1;   // not placed: the combine skips it
+    // the pick's global base (expert start + this block's offset) and weight, loaded before the ordered loop
+    const int base = ok ? start[e] + bc[(size_t)blockIdx.x * E + e] + rank : 0;
+    const float wi = ok ? w[i] : 0.0f;
     for (int s = 0; s < 32; ++s) {
         if (wid == s && ok) {
-            int pos = start[e] + bc[(size_t)blockIdx.x * E + e] + run[e] + rank;
+            int pos = base + run[e];
             o.pair_tok[pos] = i / topk;
-            o.pair_w[pos] = w[i];
+            o.pair_w[pos] = wi;
             o.pair_of[i] = pos;
         }
         __syncthreads();

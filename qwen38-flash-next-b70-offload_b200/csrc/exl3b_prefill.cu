@@ -77,7 +77,20 @@ __global__ void __launch_bounds__(1024) tiles_kernel(PrefillArgs p) {
 // One warp per sorted pick, 32 blocks of 8 warps per 256-row tile (the tile gives the expert); 8 128-blocks per warp
 // step: lane l holds 32 consecutive values (quarter l%4) of block l/4.  FWHT strides 1..16 run inside the lane,
 // strides 32 and 64 pair lanes l^1 and l^2 (the reference's butterfly order, stage by stage).
-__global__ void __launch_bounds__(256) had_in_kernel(PrefillArgs p) {
+// One in-lane butterfly stage of stride HS >= 2 over the lane's 32 values, on float2 pairs.
+template <int HS>
+__device__ __forceinline__ void had_stage2(float v[32]) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int j = (t / (HS / 2)) * (2 * HS) + (t % (HS / 2)) * 2;
+        const float2 a = make_float2(v[j], v[j + 1]), b = make_float2(v[j + HS], v[j + HS + 1]);
+        const float2 sm = f2_add(a, b), df = f2_sub(a, b);
+        v[j] = sm.x; v[j + 1] = sm.y;
+        v[j + HS] = df.x; v[j + HS + 1] = df.y;
+    }
+}
+
+__global__ void __launch_bounds__(256, 4) had_in_kernel(PrefillArgs p) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -121,23 +134,28 @@ __global__ void __launch_bounds__(256) had_in_kernel(PrefillArgs p) {
                     v[q * 8 + h] = rn16(xf * sf);
                 }
             }
+            // stride 1 inside a float2 (scalar); strides 2..16 on float2 pairs (j, j + 1), (j + hs, j + hs + 1)
 #pragma unroll
-            for (int hs = 1; hs < 32; hs <<= 1)
-#pragma unroll
-                for (int i = 0; i < 32; i += 2 * hs)
-#pragma unroll
-                    for (int j = i; j < i + hs; ++j) {
-                        const float a = v[j], b = v[j + hs];
-                        v[j] = a + b;
-                        v[j + hs] = a - b;
-                    }
+            for (int j = 0; j < 32; j += 2) {
+                const float a = v[j], b = v[j + 1];
+                v[j] = a + b;
+                v[j + 1] = a - b;
+            }
+            had_stage2<2>(v);
+            had_stage2<4>(v);
+            had_stage2<8>(v);
+            had_stage2<16>(v);
+            // strides 32, 64: the lower lane gets o + v, the upper o - v = fma(v, -1, o)
 #pragma unroll
             for (int m = 1; m <= 2; m <<= 1) {
-                const bool upper = (lane & m) != 0;
+                const float sg = (lane & m) ? -1.0f : 1.0f;
+                const float2 sg2 = make_float2(sg, sg);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
-                    v[j] = upper ? (o - v[j]) : (v[j] + o);
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, v[j], m),
+                                                 __shfl_xor_sync(0xffffffffu, v[j + 1], m));
+                    const float2 r = f2_fma(make_float2(v[j], v[j + 1]), sg2, o);
+                    v[j] = r.x; v[j + 1] = r.y;
                 }
             }
             if (act) {
