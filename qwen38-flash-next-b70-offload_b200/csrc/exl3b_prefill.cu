@@ -76,7 +76,9 @@ __global__ void __launch_bounds__(1024) tiles_kernel(PrefillArgs p) {
 // ------------------------------------------------------------------------------------------------ had_in
 // One warp per sorted pick, 32 blocks of 8 warps per 256-row tile (the tile gives the expert); 8 128-blocks per warp
 // step: lane l holds 32 consecutive values (quarter l%4) of block l/4.  FWHT strides 1..16 run inside the lane,
-// strides 32 and 64 pair lanes l^1 and l^2 (the reference's butterfly order, stage by stage).
+// strides 32 and 64 pair lanes l^1 and l^2 (the reference's butterfly order, stage by stage).  Per warp step the
+// lane's x chunk and both projections' suh chunks are loaded in one round and both products rounded to fp16 before
+// the two FWHTs: x is read once for the two projections and a pick takes two load round trips instead of four.
 // One in-lane butterfly stage of stride HS >= 2 over the lane's 32 values, on float2 pairs.
 template <int HS>
 __device__ __forceinline__ void had_stage2(float v[32]) {
@@ -90,7 +92,7 @@ __device__ __forceinline__ void had_stage2(float v[32]) {
     }
 }
 
-__global__ void __launch_bounds__(256, 4) had_in_kernel(PrefillArgs p) {
+__global__ void __launch_bounds__(256, 3) had_in_kernel(PrefillArgs p) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -108,31 +110,50 @@ __global__ void __launch_bounds__(256, 4) had_in_kernel(PrefillArgs p) {
     const int tok = p.pair_tok[pr];
     const uint16_t* xr = reinterpret_cast<const uint16_t*>(p.x) + (size_t)tok * p.xs;
     const int nblk = p.H / 128, g = lane >> 2, sub = lane & 3;
+    const uint16_t* suh = reinterpret_cast<const uint16_t*>(blob + gm.off_suh_g());   // gate; up at + H
 #pragma unroll 1
-    for (int proj = 0; proj < 2; ++proj) {
-        const uint16_t* suh = reinterpret_cast<const uint16_t*>(blob + gm.off_suh_g() + (size_t)proj * p.H * 2);
-        __half* dst = p.xh + ((size_t)proj * p.Prow + pr) * p.H;
-#pragma unroll 1
-        for (int kb0 = 0; kb0 < nblk; kb0 += 8) {
-            const int kb = kb0 + g;
-            const bool act = kb < nblk;
-            const int i0 = kb * 128 + sub * 32;
+    for (int kb0 = 0; kb0 < nblk; kb0 += 8) {
+        const int kb = kb0 + g;
+        const bool act = kb < nblk;
+        const int i0 = kb * 128 + sub * 32;
+        // the lane's 32 inputs of both projections, y = fp16(x suh): x and both suh chunks are loaded in one round,
+        // x once for the two projections
+        uint4 xv[4], sv[2][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xv[q] = act ? *reinterpret_cast<const uint4*>(xr + i0 + q * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int pj = 0; pj < 2; ++pj)
+                sv[pj][q] = act ? __ldg(reinterpret_cast<const uint4*>(suh + (size_t)pj * p.H + i0 + q * 8))
+                                : make_uint4(0, 0, 0, 0);
+        }
+        uint32_t yw[2][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t xw[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
+#pragma unroll
+            for (int pj = 0; pj < 2; ++pj) {
+                const uint32_t sw[4] = {sv[pj][q].x, sv[pj][q].y, sv[pj][q].z, sv[pj][q].w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    float x0, x1;
+                    if (p.x_bf16) { x0 = __uint_as_float(xw[h] << 16); x1 = __uint_as_float(xw[h] & 0xFFFF0000u); }
+                    else { x0 = __half2float(__ushort_as_half((unsigned short)(xw[h] & 0xFFFFu))); x1 = __half2float(__ushort_as_half((unsigned short)(xw[h] >> 16))); }
+                    const float s0 = __half2float(__ushort_as_half((unsigned short)(sw[h] & 0xFFFFu)));
+                    const float s1 = __half2float(__ushort_as_half((unsigned short)(sw[h] >> 16)));
+                    __half2 hv = __floats2half2_rn(x0 * s0, x1 * s1);
+                    yw[pj][q * 4 + h] = *reinterpret_cast<uint32_t*>(&hv);
+                }
+            }
+        }
+#pragma unroll
+        for (int proj = 0; proj < 2; ++proj) {
             float v[32];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 xv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
-                if (act) {
-                    xv = *reinterpret_cast<const uint4*>(xr + i0 + q * 8);
-                    sv = __ldg(reinterpret_cast<const uint4*>(suh + i0 + q * 8));
-                }
-                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const uint32_t xb = (xw[h >> 1] >> (16 * (h & 1))) & 0xFFFFu;
-                    const float xf = p.x_bf16 ? __uint_as_float(xb << 16) : __half2float(__ushort_as_half((unsigned short)xb));
-                    const float sf = __half2float(__ushort_as_half((unsigned short)((sw[h >> 1] >> (16 * (h & 1))) & 0xFFFFu)));
-                    v[q * 8 + h] = rn16(xf * sf);
-                }
+            for (int j = 0; j < 16; ++j) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&yw[proj][j]));
+                v[2 * j] = f.x;
+                v[2 * j + 1] = f.y;
             }
             // stride 1 inside a float2 (scalar); strides 2..16 on float2 pairs (j, j + 1), (j + hs, j + hs + 1)
 #pragma unroll
@@ -159,6 +180,7 @@ __global__ void __launch_bounds__(256, 4) had_in_kernel(PrefillArgs p) {
                 }
             }
             if (act) {
+                __half* dst = p.xh + ((size_t)proj * p.Prow + pr) * p.H;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     uint32_t ow[4];
